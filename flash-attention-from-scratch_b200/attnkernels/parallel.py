@@ -1,0 +1,105 @@
+"""Multi-GPU partitioning of the two hot paths (one process per GPU).
+
+The reference is single-GPU; this module is the B200 box layer:
+
+* Prefill shards by head (or by (batch, head) pair): the units are independent,
+  so each rank runs flash_attention on its own slice and there is no
+  collective. `head_range` / `pair_range` give a rank's contiguous share.
+
+* Long-context decode shards each sequence's context into contiguous,
+  block-aligned ranges, one per rank (`context_range`); each rank holds the
+  K/V pages of its range. A rank computes the softmax state (o, m, l) of every
+  (sequence, head) row over its range with paged_decode_partials, the states
+  are all-gathered over NCCL (the only collective: B * H * (D + 2) fp32 per
+  rank), and every rank merges them with merge_partials into the fp16 output.
+
+The compute steps are injectable so that the orchestration (packing, the
+collective, the merge layout) can be tested on CPU ranks with gloo and the CPU
+oracle; the defaults are the CUDA kernels.
+"""
+from __future__ import annotations
+
+import torch
+import torch.distributed as dist
+
+
+def shard_range(total: int, world: int, rank: int) -> tuple[int, int]:
+    """Contiguous near-equal share [begin, end) of `total` items for `rank`."""
+    if world <= 0 or not 0 <= rank < world:
+        raise ValueError(f"rank {rank} outside world of size {world}")
+    return total * rank // world, total * (rank + 1) // world
+
+
+def head_range(num_heads: int, world: int, rank: int) -> tuple[int, int]:
+    """Heads of `rank` when prefill is sharded by head (no collective)."""
+    return shard_range(num_heads, world, rank)
+
+
+def pair_range(batch: int, num_heads: int, world: int, rank: int) -> tuple[int, int]:
+    """Flattened (batch, head) pairs [begin, end) of `rank`."""
+    return shard_range(batch * num_heads, world, rank)
+
+
+def context_range(context_len: int, block_size: int, world: int, rank: int) -> tuple[int, int]:
+    """Token range [begin, end) of one sequence held by `rank`.
+
+    The sequence's blocks are split into contiguous near-equal runs, so every
+    rank owns whole blocks (the last rank's run may end in a partial block).
+    """
+    blocks = -(-context_len // block_size)
+    b0, b1 = shard_range(blocks, world, rank)
+    return min(context_len, b0 * block_size), min(context_len, b1 * block_size)
+
+
+def _gather_flat(buf: torch.Tensor, world: int, group) -> torch.Tensor:
+    out = torch.empty((world, buf.numel()), dtype=buf.dtype, device=buf.device)
+    if dist.get_backend(group) == "nccl":
+        dist.all_gather_into_tensor(out, buf, group=group)
+    else:
+        dist.all_gather(list(out.unbind(0)), buf, group=group)
+    return out
+
+
+class ContextParallelDecode:
+    """Decode with each sequence's context split across the ranks of `group`.
+
+    __call__(q, k_cache, v_cache, block_tables, context_lens, max_context_len,
+    scale=None, partition_size=None) takes this rank's cache, block tables and
+    per-sequence token counts of its range (context_lens may be 0 for some
+    sequences) and returns the merged output, fp16 [B, H, D], on every rank.
+
+    partials_fn(q, kc, vc, bt, lens, max_len, scale, partition, out=(o, m, l))
+    fills o [B, H, D], m and l [B, H] (fp32); merge_fn(o_parts, m_parts,
+    l_parts) merges [P, B, H, D] / [P, B, H] views. Defaults: the CUDA kernels.
+    """
+
+    def __init__(self, group=None, partials_fn=None, merge_fn=None):
+        self.group = group
+        if partials_fn is None or merge_fn is None:
+            from . import merge_partials, paged_decode_partials
+            partials_fn = partials_fn or paged_decode_partials
+            merge_fn = merge_fn or merge_partials
+        self.partials_fn = partials_fn
+        self.merge_fn = merge_fn
+
+    def __call__(self, q, k_cache, v_cache, block_tables, context_lens, max_context_len,
+                 scale=None, partition_size=None):
+        world = dist.get_world_size(self.group)
+        if q.dim() == 4:
+            q = q.reshape(q.shape[0], q.shape[1], q.shape[3])
+        B, H, D = q.shape
+        rows = B * H
+        # One fp32 buffer per rank: o [rows, D], m [rows], l [rows], padded to
+        # 16 bytes so every part's o rows stay 16-byte aligned after the gather.
+        stride = -(-(rows * (D + 2)) // 4) * 4
+        buf = torch.empty(stride, dtype=torch.float32, device=q.device)
+        o = buf[: rows * D].view(B, H, D)
+        m = buf[rows * D: rows * (D + 1)].view(B, H)
+        l = buf[rows * (D + 1): rows * (D + 2)].view(B, H)
+        self.partials_fn(q, k_cache, v_cache, block_tables, context_lens, max_context_len,
+                         scale, partition_size, out=(o, m, l))
+        gathered = _gather_flat(buf, world, self.group)
+        o_parts = gathered[:, : rows * D].view(world, B, H, D)
+        m_parts = gathered[:, rows * D: rows * (D + 1)].view(world, B, H)
+        l_parts = gathered[:, rows * (D + 1): rows * (D + 2)].view(world, B, H)
+        return self.merge_fn(o_parts, m_parts, l_parts)

@@ -1,0 +1,643 @@
+// Paged-KV decode attention with split-K ("flash-decoding") and the merge of
+// the split partials.
+//
+// Semantics follow the reference's paged_decode_kernel / paged_reduce_kernel
+// (attnkernels/csrc/paged_decode.cu:39-216): sequence b has context_lens[b]
+// tokens; token t lives in physical block block_tables[b][t / bs] at row
+// t % bs of cache [num_blocks, H_kv, bs, D]; query head h reads kv head
+// h / G; the context is cut into partitions of `partition` tokens; each
+// partition yields (o = acc / l, m, l) with scores in log2 units
+// (q pre-multiplied by scale * log2 e); the merge is
+//     M = max_s m_s,  w_s = l_s 2^(m_s - M),  O = sum_s w_s o_s / sum_s w_s.
+//
+// The B200 design is different from the reference's one-CTA-per-split grid:
+//   * A persistent grid of one CTA per SM, 8 warps per CTA. Each warp is an
+//     independent pipeline that owns whole work units (sequence, kv head,
+//     split) and fetches the next unit from an atomic counter, so no CTA-wide
+//     barrier is ever taken inside the main loop and the short final splits of
+//     ragged sequences balance across warps.
+//   * K, V and q move by 1-D bulk copies (cp.async.bulk, the TMA engine) of
+//     whole page runs into a per-warp ring of 16-token stages signalled by
+//     mbarriers: a page of one head is bs * D * 2 contiguous bytes (4 KB at
+//     bs = 16, D = 128), so every copy is a long contiguous DRAM burst and
+//     about 190 KB per SM is in flight. The producer runs `STAGES` stages
+//     ahead of the consumer, across unit boundaries.
+//   * No tensor cores (one query row per head): scores with 8 lanes per token
+//     and 16-byte shared-memory loads, an online softmax per 16-token stage,
+//     and P V with each lane owning D / 32 output columns. Grouped-query heads
+//     (G = H / H_kv) share every K/V byte.
+#include <algorithm>
+#include <mutex>
+
+#include "common.cuh"
+#include "launch.h"
+
+namespace fab {
+namespace {
+
+constexpr int kTok = 16;       // tokens per pipeline stage
+constexpr int kWarps = 8;      // warps per CTA
+constexpr int kThreads = kWarps * 32;
+constexpr int kMaxBatch = 2048;  // sequences per launch (their prefix sums live in smem)
+
+enum : unsigned int { kSiteDecodeWait = 201, kSiteDecodeDrain = 202, kSiteBadBlock = 203 };
+
+template <int D, int G>
+struct DecCfg {
+  static constexpr int ROW = D * 2;                        // bytes of one token of one head
+  static constexpr int KV = kTok * ROW;                    // K (or V) bytes of one stage
+  static constexpr int QB = (G * D * 2 + 15) / 16 * 16;    // q bytes of one unit
+  static constexpr int STAGE = 2 * KV + QB;
+  static constexpr int BUDGET = 196 * 1024 / kWarps;       // ring bytes per warp
+  static constexpr int STAGES = std::min(6, BUDGET / STAGE);
+  static constexpr int RING = STAGES * STAGE;
+  static constexpr int BAR_OFF = kWarps * RING;
+  static constexpr int META_OFF = BAR_OFF + kWarps * STAGES * 8;
+  static constexpr int PREFIX_OFF = META_OFF + kWarps * STAGES * 16;
+  static constexpr int CTX_OFF = PREFIX_OFF + (kMaxBatch + 1) * 4;
+  static constexpr int SMEM = CTX_OFF + kMaxBatch * 4 + 16;
+  static constexpr int E = D / 8;    // K elements per lane in the score phase
+  static constexpr int DV = D / 32;  // output columns per lane
+  static_assert(STAGES >= 2, "ring needs two stages");
+  static_assert(SMEM <= 227 * 1024, "shared memory per CTA");
+};
+
+struct DecParams {
+  const __half* q;
+  const __half* kc;
+  const __half* vc;
+  const int* bt;
+  const int* ctx;
+  __half* out;     // fp16 [batch, hq, D]: rows of sequences with one split (direct_out)
+  float* o_part;   // fp32 [batch * hq, num_splits, D]
+  float* m_part;   // fp32 [batch * hq, num_splits]
+  float* l_part;
+  unsigned int* counter;  // work counter, zero at launch
+  DeviceStatus* status;
+  unsigned long long timeout_ns;
+  long long block_stride;  // elements between physical blocks (hkv * bs * D)
+  int batch, hq, hkv, bs, max_blocks, partition, num_splits;
+  int num_blocks;  // physical blocks in the cache: block ids outside [0, num_blocks) are rejected
+  int direct_out;  // 1: a sequence with a single split writes its fp16 row directly
+  float scale_log2;
+};
+
+
+// 8 fp16 -> 8 fp32 from a 16-byte shared-memory load.
+__device__ __forceinline__ void load8_f32(const __half* src, float* dst) {
+  const uint4 raw = *reinterpret_cast<const uint4*>(src);
+  const __half2* h = reinterpret_cast<const __half2*>(&raw);
+#pragma unroll
+  for (int i = 0; i < 4; ++i) {
+    const float2 f = __half22float2(h[i]);
+    dst[2 * i] = f.x;
+    dst[2 * i + 1] = f.y;
+  }
+}
+
+template <int D, int G>
+__global__ void __launch_bounds__(kThreads, 1) paged_decode_kernel(const DecParams p) {
+  using C = DecCfg<D, G>;
+  extern __shared__ __align__(128) uint8_t smem[];
+  const int warp = threadIdx.x >> 5;
+  const int lane = threadIdx.x & 31;
+  const int grp = lane >> 3;  // token of a 4-token step in the score phase
+  const int l8 = lane & 7;    // 16-byte column chunk of that token
+  uint8_t* ring = smem + warp * C::RING;
+  uint64_t* full = reinterpret_cast<uint64_t*>(smem + C::BAR_OFF) + warp * C::STAGES;
+  int4* meta = reinterpret_cast<int4*>(smem + C::META_OFF) + warp * C::STAGES;
+  int* prefix = reinterpret_cast<int*>(smem + C::PREFIX_OFF);
+  int* ctx_s = reinterpret_cast<int*>(smem + C::CTX_OFF);
+  volatile int* abort_flag = reinterpret_cast<volatile int*>(smem + C::SMEM - 16);
+
+  // Context lengths and the prefix sums of the splits per sequence: active
+  // (sequence, split) pairs are numbered densely, v in [0, prefix[batch]).
+  for (int b = threadIdx.x; b < p.batch; b += kThreads) ctx_s[b] = max(p.ctx[b], 0);
+  if (threadIdx.x < kWarps * C::STAGES)
+    mbar_init(reinterpret_cast<uint64_t*>(smem + C::BAR_OFF) + threadIdx.x, 1);
+  if (threadIdx.x == 0) {
+    *abort_flag = 0;
+    fence_mbar_init();
+  }
+  __syncthreads();
+  if (warp == 0) {
+    const int per = (p.batch + 31) / 32;
+    const int b0 = lane * per;
+    int sum = 0;
+    for (int i = 0; i < per; ++i) {
+      const int b = b0 + i;
+      if (b < p.batch) sum += min((ctx_s[b] + p.partition - 1) / p.partition, p.num_splits);
+    }
+    int incl = sum;
+#pragma unroll
+    for (int o = 1; o < 32; o <<= 1) {
+      const int y = __shfl_up_sync(0xffffffffu, incl, o);
+      if (lane >= o) incl += y;
+    }
+    int run = incl - sum;
+    for (int i = 0; i < per; ++i) {
+      const int b = b0 + i;
+      if (b < p.batch) {
+        prefix[b] = run;
+        run += min((ctx_s[b] + p.partition - 1) / p.partition, p.num_splits);
+      }
+    }
+    if (lane == 31) prefix[p.batch] = incl;
+  }
+  __syncthreads();
+  // Without a merge pass, rows of empty sequences are written here (zeros).
+  if (p.direct_out && p.num_splits == 1 && blockIdx.x == 0) {
+    for (int b = warp; b < p.batch; b += kWarps) {
+      if (ctx_s[b] != 0) continue;
+      for (int i = lane; i < p.hq * D / 2; i += 32)
+        reinterpret_cast<uint32_t*>(p.out + static_cast<size_t>(b) * p.hq * D)[i] = 0u;
+    }
+  }
+  const int total_units = prefix[p.batch] * p.hkv;
+
+  // ---------------------------------------------------------- producer state
+  int pu = -1, pb = 0, pkvh = 0, psplit = 0, pstart = 0, pend = 0, pst = 0, pnst = 0;
+  int bt_base = 0, bt_reg = 0;
+  unsigned int nxt = 0;  // next unit id (valid in lane 0), fetched one unit ahead
+  unsigned int p_item = 0, c_item = 0;
+
+  auto advance = [&]() {
+    const int u = static_cast<int>(__shfl_sync(0xffffffffu, nxt, 0));
+    if (u >= total_units) {
+      pu = -1;
+      return;
+    }
+    pu = u;
+    const int v = u / p.hkv;
+    pkvh = u - v * p.hkv;
+    int lo = 0, hi = p.batch - 1;  // last sequence whose first pair is <= v
+    while (lo < hi) {
+      const int mid = (lo + hi + 1) >> 1;
+      if (prefix[mid] <= v) lo = mid; else hi = mid - 1;
+    }
+    pb = lo;
+    psplit = v - prefix[lo];
+    pstart = psplit * p.partition;
+    pend = min(ctx_s[pb], pstart + p.partition);
+    pst = 0;
+    pnst = (pend - pstart + kTok - 1) / kTok;
+    bt_base = -(1 << 30);
+    if (lane == 0) nxt = atomicAdd(p.counter, 1u);
+  };
+
+  // Issue the copies of the producer's next stage into its ring slot.
+  auto produce = [&]() {
+    if (pu < 0) return;
+    const unsigned int slot = p_item % C::STAGES;
+    uint8_t* st = ring + slot * C::STAGE;
+    uint64_t* bar = full + slot;
+    const int t0 = pstart + pst * kTok;
+    const int nt = min(kTok, pend - t0);
+    if (lane == 0)
+      mbar_arrive_expect_tx(bar, 2 * nt * C::ROW + (pst == 0 ? G * D * 2 : 0));
+    const int* btrow = p.bt + static_cast<size_t>(pb) * p.max_blocks;
+    for (int t = t0; t < t0 + nt;) {
+      const int pg = t / p.bs;
+      const int off = t - pg * p.bs;
+      const int rows = min(p.bs - off, t0 + nt - t);
+      if (pg - bt_base >= 32 || pg < bt_base) {  // next 32 block-table entries, one per lane
+        bt_base = pg;
+        bt_reg = (pg + lane < p.max_blocks) ? btrow[pg + lane] : 0;
+      }
+      int page = __shfl_sync(0xffffffffu, bt_reg, pg - bt_base);
+      if (page < 0 || page >= p.num_blocks) {  // never read outside the cache
+        if (lane == 0) report_status(p.status, 2u /* ATTN_DEVICE_BAD_BLOCK */, kSiteBadBlock);
+        page = 0;
+      }
+      if (lane == 0) {
+        const size_t eoff = static_cast<size_t>(page) * p.block_stride +
+                            (static_cast<size_t>(pkvh) * p.bs + off) * D;
+        const uint32_t dst = static_cast<uint32_t>(t - t0) * C::ROW;
+        bulk_g2s(st + dst, p.kc + eoff, rows * C::ROW, bar);
+        bulk_g2s(st + C::KV + dst, p.vc + eoff, rows * C::ROW, bar);
+      }
+      t += rows;
+    }
+    if (lane == 0) {
+      if (pst == 0)
+        bulk_g2s(st + 2 * C::KV, p.q + (static_cast<size_t>(pb) * p.hq + pkvh * G) * D,
+                 G * D * 2, bar);
+      meta[slot] = make_int4(pb, pkvh, psplit,
+                             nt | ((pst == 0) ? 32 : 0) | ((pst == pnst - 1) ? 64 : 0));
+    }
+    ++p_item;
+    if (++pst == pnst) advance();
+  };
+
+  // ---------------------------------------------------------- consumer state
+  float qf[G][C::E];  // q * scale * log2(e): the 16 (or 8) elements this lane multiplies
+  float m[G], l[G];
+  float acc[G][C::DV];
+
+  auto consume = [&]() -> bool {
+    const unsigned int slot = c_item % C::STAGES;
+    const uint32_t parity = (c_item / C::STAGES) & 1u;
+    const bool ok = mbar_wait(full + slot, parity, abort_flag, p.status, kSiteDecodeWait,
+                              p.timeout_ns);
+    if (!__all_sync(0xffffffffu, ok)) return false;
+    const int4 md = meta[slot];
+    const uint8_t* st = ring + slot * C::STAGE;
+    const int nt = md.w & 31;
+    if (md.w & 32) {
+      const __half* qs = reinterpret_cast<const __half*>(st + 2 * C::KV);
+#pragma unroll
+      for (int g = 0; g < G; ++g) {
+#pragma unroll
+        for (int e8 = 0; e8 < C::E / 8; ++e8) {
+          load8_f32(qs + g * D + e8 * 64 + l8 * 8, &qf[g][e8 * 8]);
+#pragma unroll
+          for (int i = 0; i < 8; ++i) qf[g][e8 * 8 + i] *= p.scale_log2;
+        }
+        m[g] = -INFINITY;
+        l[g] = 0.f;
+#pragma unroll
+        for (int j = 0; j < C::DV; ++j) acc[g][j] = 0.f;
+      }
+    }
+    // Scores: token 4 * step + grp, 8 lanes per token.
+    float s[kTok / 4][G];
+    const __half* kst = reinterpret_cast<const __half*>(st);
+#pragma unroll
+    for (int step = 0; step < kTok / 4; ++step) {
+      const int t = step * 4 + grp;
+      float kf[C::E];
+#pragma unroll
+      for (int e8 = 0; e8 < C::E / 8; ++e8) load8_f32(kst + t * D + e8 * 64 + l8 * 8, &kf[e8 * 8]);
+#pragma unroll
+      for (int g = 0; g < G; ++g) {
+        float dot = 0.f;
+#pragma unroll
+        for (int e = 0; e < C::E; ++e) dot = fmaf(qf[g][e], kf[e], dot);
+        dot += __shfl_xor_sync(0xffffffffu, dot, 4);
+        dot += __shfl_xor_sync(0xffffffffu, dot, 2);
+        dot += __shfl_xor_sync(0xffffffffu, dot, 1);
+        s[step][g] = (t < nt) ? dot : -INFINITY;
+      }
+    }
+    // Online softmax over the stage's tokens (the 4 lane groups hold 4 tokens each).
+#pragma unroll
+    for (int g = 0; g < G; ++g) {
+      float mx = fmaxf(fmaxf(s[0][g], s[1][g]), fmaxf(s[2][g], s[3][g]));
+      mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, 8));
+      mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, 16));
+      const float mn = fmaxf(m[g], mx);
+      const float alpha = fast_exp2(m[g] - mn);
+      float ps = 0.f;
+#pragma unroll
+      for (int step = 0; step < kTok / 4; ++step) {
+        s[step][g] = fast_exp2(s[step][g] - mn);
+        ps += s[step][g];
+      }
+      ps += __shfl_xor_sync(0xffffffffu, ps, 8);
+      ps += __shfl_xor_sync(0xffffffffu, ps, 16);
+      l[g] = l[g] * alpha + ps;
+      m[g] = mn;
+#pragma unroll
+      for (int j = 0; j < C::DV; ++j) acc[g][j] *= alpha;
+    }
+    // P V: lane owns output columns [lane * DV, lane * DV + DV).
+    const __half* vst = reinterpret_cast<const __half*>(st + C::KV) + lane * C::DV;
+#pragma unroll
+    for (int t = 0; t < kTok; ++t) {
+      if (t < nt) {
+        float vf[C::DV];
+        if constexpr (C::DV == 4) {
+          const uint2 raw = *reinterpret_cast<const uint2*>(vst + t * D);
+          const float2 a = __half22float2(*reinterpret_cast<const __half2*>(&raw.x));
+          const float2 b = __half22float2(*reinterpret_cast<const __half2*>(&raw.y));
+          vf[0] = a.x; vf[1] = a.y; vf[2] = b.x; vf[3] = b.y;
+        } else {
+          const float2 a = __half22float2(*reinterpret_cast<const __half2*>(vst + t * D));
+          vf[0] = a.x; vf[1] = a.y;
+        }
+#pragma unroll
+        for (int g = 0; g < G; ++g) {
+          const float pt = __shfl_sync(0xffffffffu, s[t >> 2][g], (t & 3) * 8);
+#pragma unroll
+          for (int j = 0; j < C::DV; ++j) acc[g][j] = fmaf(pt, vf[j], acc[g][j]);
+        }
+      }
+    }
+    __syncwarp();
+    if (md.w & 64) {
+      const int b = md.x, kvh = md.y, split = md.z;
+      const int ns = min((ctx_s[b] + p.partition - 1) / p.partition, p.num_splits);
+#pragma unroll
+      for (int g = 0; g < G; ++g) {
+        const float inv = 1.f / l[g];
+        const size_t row = static_cast<size_t>(b) * p.hq + kvh * G + g;
+        if (p.direct_out && ns == 1) {
+          __half* dst = p.out + row * D + lane * C::DV;
+          if constexpr (C::DV == 4) {
+            *reinterpret_cast<uint2*>(dst) = make_uint2(pack_half2(acc[g][0] * inv, acc[g][1] * inv),
+                                                        pack_half2(acc[g][2] * inv, acc[g][3] * inv));
+          } else {
+            *reinterpret_cast<uint32_t*>(dst) = pack_half2(acc[g][0] * inv, acc[g][1] * inv);
+          }
+        } else {
+          const size_t pr = row * p.num_splits + split;
+          float* dst = p.o_part + pr * D + lane * C::DV;
+          if constexpr (C::DV == 4) {
+            *reinterpret_cast<float4*>(dst) =
+                make_float4(acc[g][0] * inv, acc[g][1] * inv, acc[g][2] * inv, acc[g][3] * inv);
+          } else {
+            *reinterpret_cast<float2*>(dst) = make_float2(acc[g][0] * inv, acc[g][1] * inv);
+          }
+          if (lane == 0) {
+            p.m_part[pr] = m[g];
+            p.l_part[pr] = l[g];
+          }
+        }
+      }
+    }
+    ++c_item;
+    return true;
+  };
+
+  if (lane == 0) nxt = atomicAdd(p.counter, 1u);
+  advance();
+  for (int i = 0; i < C::STAGES; ++i) produce();
+  while (c_item < p_item) {
+    if (!consume()) break;
+    // The slot just read is refilled by the async proxy.
+    asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+    produce();
+  }
+  // Never exit with a copy in flight (only reached with copies pending after a timeout).
+  while (c_item < p_item) {
+    const unsigned int slot = c_item % C::STAGES;
+    mbar_wait(full + slot, (c_item / C::STAGES) & 1u, nullptr, p.status, kSiteDecodeDrain,
+              p.timeout_ns);
+    ++c_item;
+  }
+}
+
+
+struct MergeParams {
+  const float* o;
+  const float* m;
+  const float* l;
+  const int* ctx;  // non-null: row r has min(ceil(ctx[r / hq] / partition), num_parts) parts
+  long long rows;
+  long long o_row_stride, o_part_stride, ml_row_stride, ml_part_stride;
+  int hq, partition, num_parts;
+  int skip_single;  // rows with exactly one part were written by the decode kernel
+  __half* out16;    // fp16 [rows, D], or else the merged partial state:
+  float* out_o;     // fp32 [rows, D]
+  float* out_m;     // fp32 [rows]
+  float* out_l;
+};
+
+// One warp per row; lane owns D / 32 consecutive columns.
+template <int D>
+__global__ void __launch_bounds__(256) merge_partials_kernel(const MergeParams p) {
+  constexpr int DV = D / 32;
+  const long long row = static_cast<long long>(blockIdx.x) * 8 + (threadIdx.x >> 5);
+  const int lane = threadIdx.x & 31;
+  if (row >= p.rows) return;
+  int ns = p.num_parts;
+  if (p.ctx != nullptr) {
+    const int c = max(p.ctx[row / p.hq], 0);
+    ns = min((c + p.partition - 1) / p.partition, p.num_parts);
+  }
+  if (p.skip_single && ns == 1) return;
+  const float* mrow = p.m + row * p.ml_row_stride;
+  const float* lrow = p.l + row * p.ml_row_stride;
+  float mx = -INFINITY;
+  for (int s = lane; s < ns; s += 32) mx = fmaxf(mx, mrow[s * p.ml_part_stride]);
+  mx = warp_max(mx);
+  float num[DV];
+#pragma unroll
+  for (int j = 0; j < DV; ++j) num[j] = 0.f;
+  float den = 0.f;
+  if (mx != -INFINITY) {
+    const float* orow = p.o + row * p.o_row_stride + lane * DV;
+    for (int s = 0; s < ns; ++s) {
+      const float w = lrow[s * p.ml_part_stride] * fast_exp2(mrow[s * p.ml_part_stride] - mx);
+      den += w;
+      const float* src = orow + s * p.o_part_stride;
+      if constexpr (DV == 4) {
+        const float4 v = *reinterpret_cast<const float4*>(src);
+        num[0] = fmaf(w, v.x, num[0]);
+        num[1] = fmaf(w, v.y, num[1]);
+        num[2] = fmaf(w, v.z, num[2]);
+        num[3] = fmaf(w, v.w, num[3]);
+      } else {
+        const float2 v = *reinterpret_cast<const float2*>(src);
+        num[0] = fmaf(w, v.x, num[0]);
+        num[1] = fmaf(w, v.y, num[1]);
+      }
+    }
+  }
+  const float inv = den > 0.f ? 1.f / den : 0.f;
+  if (p.out16 != nullptr) {
+    __half* dst = p.out16 + row * D + lane * DV;
+    if constexpr (DV == 4) {
+      *reinterpret_cast<uint2*>(dst) =
+          make_uint2(pack_half2(num[0] * inv, num[1] * inv), pack_half2(num[2] * inv, num[3] * inv));
+    } else {
+      *reinterpret_cast<uint32_t*>(dst) = pack_half2(num[0] * inv, num[1] * inv);
+    }
+  } else {
+    float* dst = p.out_o + row * D + lane * DV;
+#pragma unroll
+    for (int j = 0; j < DV; ++j) dst[j] = num[j] * inv;
+    if (lane == 0) {
+      p.out_m[row] = mx;
+      p.out_l[row] = den;
+    }
+  }
+}
+
+// Waits on an mbarrier that nothing arrives on: the bounded wait must give up,
+// record ATTN_DEVICE_WAIT_TIMEOUT and let the kernel finish.
+__global__ void wait_selftest_kernel(DeviceStatus* status, unsigned long long timeout_ns) {
+  __shared__ uint64_t bar;
+  __shared__ int abort_flag;
+  if (threadIdx.x == 0) {
+    mbar_init(&bar, 1);
+    abort_flag = 0;
+    fence_mbar_init();
+  }
+  __syncthreads();
+  mbar_wait(&bar, 0, &abort_flag, status, 301u, timeout_ns);
+  __syncthreads();
+}
+
+size_t align256(size_t x) { return (x + 255) & ~static_cast<size_t>(255); }
+
+struct DecodeWorkspace {
+  unsigned int* counters;
+  float* o_part;
+  float* m_part;
+  float* l_part;
+  size_t bytes;
+};
+
+DecodeWorkspace carve_workspace(void* base, int64_t batch, int64_t hq, int64_t d,
+                                int64_t num_splits) {
+  DecodeWorkspace w;
+  const int64_t chunks = (batch + kMaxBatch - 1) / kMaxBatch;
+  const size_t rows = static_cast<size_t>(batch) * hq;
+  const size_t c_bytes = align256(static_cast<size_t>(chunks) * 4);
+  const size_t o_bytes = align256(rows * num_splits * d * 4);
+  const size_t ml_bytes = align256(rows * num_splits * 4);
+  uint8_t* b = static_cast<uint8_t*>(base);
+  w.counters = reinterpret_cast<unsigned int*>(b);
+  w.o_part = reinterpret_cast<float*>(b + c_bytes);
+  w.m_part = reinterpret_cast<float*>(b + c_bytes + o_bytes);
+  w.l_part = reinterpret_cast<float*>(b + c_bytes + o_bytes + ml_bytes);
+  w.bytes = c_bytes + o_bytes + 2 * ml_bytes;
+  return w;
+}
+
+int64_t splits_of(int64_t max_ctx, int64_t partition) {
+  return max_ctx > 0 ? (max_ctx + partition - 1) / partition : 0;
+}
+
+template <int D, int G>
+cudaError_t launch_decode_kernel(const DecParams& prm, int64_t upper_units, const LaunchCtx& ctx) {
+  using C = DecCfg<D, G>;
+  auto kern = paged_decode_kernel<D, G>;
+  static std::once_flag once;
+  static cudaError_t attr_err = cudaSuccess;
+  std::call_once(once, [&] {
+    attr_err = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, C::SMEM);
+  });
+  if (attr_err != cudaSuccess) return attr_err;
+  const int64_t want = (upper_units + kWarps - 1) / kWarps;
+  const int grid = static_cast<int>(std::max<int64_t>(1, std::min<int64_t>(ctx.sm_count, want)));
+  kern<<<grid, kThreads, C::SMEM, ctx.stream>>>(prm);
+  return cudaGetLastError();
+}
+
+template <int D>
+cudaError_t dispatch_group(int g, const DecParams& prm, int64_t upper, const LaunchCtx& ctx) {
+  switch (g) {
+    case 1: return launch_decode_kernel<D, 1>(prm, upper, ctx);
+    case 2: return launch_decode_kernel<D, 2>(prm, upper, ctx);
+    case 4: return launch_decode_kernel<D, 4>(prm, upper, ctx);
+    case 8: return launch_decode_kernel<D, 8>(prm, upper, ctx);
+    default: return cudaErrorInvalidValue;
+  }
+}
+
+cudaError_t launch_merge_impl(const MergeParams& mp, int d, cudaStream_t stream) {
+  if (mp.rows == 0) return cudaSuccess;
+  const unsigned grid = static_cast<unsigned>((mp.rows + 7) / 8);
+  if (d == 64)
+    merge_partials_kernel<64><<<grid, 256, 0, stream>>>(mp);
+  else
+    merge_partials_kernel<128><<<grid, 256, 0, stream>>>(mp);
+  return cudaGetLastError();
+}
+
+}  // namespace
+
+size_t decode_workspace_bytes(int64_t batch, int64_t hq, int64_t d, int64_t max_ctx,
+                              int64_t partition) {
+  return carve_workspace(nullptr, batch, hq, d, splits_of(max_ctx, partition)).bytes;
+}
+
+cudaError_t launch_paged_decode(const DecodeArgs& a, bool partials_mode, const LaunchCtx& ctx) {
+  const int64_t num_splits = splits_of(a.max_ctx, a.partition);
+  const int64_t rows = a.batch * a.hq;
+  DecodeWorkspace w = carve_workspace(a.workspace, a.batch, a.hq, a.d, num_splits);
+  if (num_splits == 0 && !partials_mode) {
+    return cudaMemsetAsync(a.out, 0, static_cast<size_t>(rows) * a.d * 2, ctx.stream);
+  }
+  if (num_splits > 0) {
+    const int64_t chunks = (a.batch + kMaxBatch - 1) / kMaxBatch;
+    cudaError_t e = cudaMemsetAsync(w.counters, 0, static_cast<size_t>(chunks) * 4, ctx.stream);
+    if (e != cudaSuccess) return e;
+    const int g = static_cast<int>(a.hq / a.hkv);
+    for (int64_t c = 0; c < chunks; ++c) {
+      const int64_t b0 = c * kMaxBatch;
+      const int64_t nb = std::min<int64_t>(kMaxBatch, a.batch - b0);
+      DecParams prm;
+      prm.q = static_cast<const __half*>(a.q) + b0 * a.hq * a.d;
+      prm.kc = static_cast<const __half*>(a.k_cache);
+      prm.vc = static_cast<const __half*>(a.v_cache);
+      prm.bt = a.block_tables + b0 * a.max_blocks;
+      prm.ctx = a.context_lens + b0;
+      prm.out = partials_mode ? nullptr : static_cast<__half*>(a.out) + b0 * a.hq * a.d;
+      prm.o_part = w.o_part + b0 * a.hq * num_splits * a.d;
+      prm.m_part = w.m_part + b0 * a.hq * num_splits;
+      prm.l_part = w.l_part + b0 * a.hq * num_splits;
+      prm.counter = w.counters + c;
+      prm.status = ctx.status;
+      prm.timeout_ns = ctx.timeout_ns;
+      prm.block_stride = a.hkv * a.bs * a.d;
+      prm.batch = static_cast<int>(nb);
+      prm.hq = static_cast<int>(a.hq);
+      prm.hkv = static_cast<int>(a.hkv);
+      prm.bs = static_cast<int>(a.bs);
+      prm.max_blocks = static_cast<int>(a.max_blocks);
+      prm.partition = static_cast<int>(a.partition);
+      prm.num_blocks = static_cast<int>(a.num_blocks);
+      prm.num_splits = static_cast<int>(num_splits);
+      prm.direct_out = partials_mode ? 0 : 1;
+      prm.scale_log2 = a.scale * kLog2e;
+      const int64_t upper = nb * a.hkv * num_splits;
+      e = (a.d == 64) ? dispatch_group<64>(g, prm, upper, ctx)
+                      : dispatch_group<128>(g, prm, upper, ctx);
+      if (e != cudaSuccess) return e;
+    }
+  }
+  if (!partials_mode && num_splits <= 1) return cudaSuccess;
+  MergeParams mp;
+  mp.o = w.o_part;
+  mp.m = w.m_part;
+  mp.l = w.l_part;
+  mp.ctx = a.context_lens;
+  mp.rows = rows;
+  mp.o_row_stride = num_splits * a.d;
+  mp.o_part_stride = a.d;
+  mp.ml_row_stride = num_splits;
+  mp.ml_part_stride = 1;
+  mp.hq = static_cast<int>(a.hq);
+  mp.partition = static_cast<int>(a.partition);
+  mp.num_parts = static_cast<int>(num_splits);
+  mp.skip_single = partials_mode ? 0 : 1;
+  mp.out16 = partials_mode ? nullptr : static_cast<__half*>(a.out);
+  mp.out_o = a.o_final;
+  mp.out_m = a.m_final;
+  mp.out_l = a.l_final;
+  return launch_merge_impl(mp, static_cast<int>(a.d), ctx.stream);
+}
+
+cudaError_t launch_merge(const float* o_parts, const float* m_parts, const float* l_parts,
+                         int64_t num_parts, int64_t rows, int64_t d, int64_t o_part_stride,
+                         int64_t ml_part_stride, void* out, const LaunchCtx& ctx) {
+  MergeParams mp;
+  mp.o = o_parts;
+  mp.m = m_parts;
+  mp.l = l_parts;
+  mp.ctx = nullptr;
+  mp.rows = rows;
+  mp.o_row_stride = d;
+  mp.o_part_stride = o_part_stride;
+  mp.ml_row_stride = 1;
+  mp.ml_part_stride = ml_part_stride;
+  mp.hq = 1;
+  mp.partition = 1;
+  mp.num_parts = static_cast<int>(num_parts);
+  mp.skip_single = 0;
+  mp.out16 = static_cast<__half*>(out);
+  mp.out_o = nullptr;
+  mp.out_m = nullptr;
+  mp.out_l = nullptr;
+  return launch_merge_impl(mp, static_cast<int>(d), ctx.stream);
+}
+
+cudaError_t launch_selftest_wait(unsigned long long timeout_ns, const LaunchCtx& ctx) {
+  wait_selftest_kernel<<<1, 32, 0, ctx.stream>>>(ctx.status, timeout_ns);
+  return cudaGetLastError();
+}
+
+}  // namespace fab

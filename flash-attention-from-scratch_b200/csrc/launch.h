@@ -1,0 +1,65 @@
+// Host-side launchers of the kernels, called by the C ABI in api.cu. Each
+// returns cudaSuccess or the launch error; argument checking is done by the
+// caller.
+#pragma once
+
+#include <cstddef>
+#include <cstdint>
+#include <string>
+
+#include <cuda_runtime.h>
+
+#include "common.cuh"
+
+namespace fab {
+
+struct LaunchCtx {
+  cudaStream_t stream;
+  DeviceStatus* status;          // device status word of the current device
+  unsigned long long timeout_ns; // limit of every bounded wait
+  int sm_count;                  // SMs of the current device
+};
+
+// tcgen05 FlashAttention forward; q, k, v, o fp16 [bh, n, d], d in {64, 128}.
+cudaError_t launch_flash_tc(const void* q, const void* k, const void* v, void* o, int64_t bh,
+                            int64_t n, int d, bool causal, float scale, const LaunchCtx& ctx,
+                            std::string* err);
+
+// CUDA-core tiled online-softmax attention, same layout.
+cudaError_t launch_flash_simt(const void* q, const void* k, const void* v, void* o, int64_t bh,
+                              int64_t n, int d, bool causal, float scale, const LaunchCtx& ctx);
+
+// Three-kernel attention with fp32 scores in `scores` ([bh, n, n]).
+cudaError_t launch_naive(const void* q, const void* k, const void* v, void* o, float* scores,
+                         int64_t bh, int64_t n, int d, bool causal, float scale,
+                         const LaunchCtx& ctx);
+
+struct DecodeArgs {
+  const void* q;          // fp16 [batch, hq, d]
+  const void* k_cache;    // fp16 [num_blocks, hkv, bs, d]
+  const void* v_cache;
+  const int32_t* block_tables;  // [batch, max_blocks]
+  const int32_t* context_lens;  // [batch]
+  void* out;              // fp16 [batch, hq, d]           (final mode)
+  float* o_final;         // fp32 [batch, hq, d] partials   (partials mode)
+  float* m_final;         // fp32 [batch, hq]
+  float* l_final;
+  int64_t batch, hq, hkv, d, bs, num_blocks, max_blocks, max_ctx, partition;
+  float scale;
+  void* workspace;
+  size_t workspace_bytes;
+};
+
+// Workspace layout of the decode path.
+size_t decode_workspace_bytes(int64_t batch, int64_t hq, int64_t d, int64_t max_ctx,
+                              int64_t partition);
+
+cudaError_t launch_paged_decode(const DecodeArgs& a, bool partials_mode, const LaunchCtx& ctx);
+
+cudaError_t launch_merge(const float* o_parts, const float* m_parts, const float* l_parts,
+                         int64_t num_parts, int64_t rows, int64_t d, int64_t o_part_stride,
+                         int64_t ml_part_stride, void* out, const LaunchCtx& ctx);
+
+cudaError_t launch_selftest_wait(unsigned long long timeout_ns, const LaunchCtx& ctx);
+
+}  // namespace fab

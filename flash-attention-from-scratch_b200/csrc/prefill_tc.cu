@@ -1,0 +1,495 @@
+// FlashAttention forward on the sm_100a tensor cores.
+//
+// Same mathematics as the reference's flash_wmma_kernel
+// (attnkernels/csrc/flash_wmma.cu:53-219): per query row an online softmax in
+// base 2 (m_new = max(m, rowmax), alpha = 2^(m - m_new), l = l alpha + sum p,
+// O = O alpha + P V, O / l at the end), fp32 scores, P rounded to fp16 for the
+// second product, top-left causal mask (key > query masked) and masking of keys
+// past the sequence end. The execution model is Blackwell's:
+//
+//   * A CTA owns NQ = 2 query tiles of 128 rows of one (batch, head) and walks
+//     the key/value tiles of 128 rows. Warp roles:
+//       warps 0-3, 4-7  softmax warpgroups, one per query tile, one thread per row
+//       warp  8         MMA issuer (one thread) + tensor-memory allocator
+//       warp  9         TMA producer (one thread)
+//   * Q, K, V tiles arrive by TMA (128-byte swizzle, zero fill past the end of
+//     the sequence) into a 2-stage K ring and a 2-stage V ring.
+//   * S_i = Q_i K^T is a tcgen05.mma with both operands in shared memory and the
+//     fp32 result in tensor memory (TMEM). The softmax thread of row r reads row
+//     r of S_i from TMEM lane r, writes P as packed fp16 back over the first 64
+//     columns of S_i, and O_i += P_i V is a tcgen05.mma with A = P read from
+//     TMEM and B = V from shared memory (MN-major), accumulating in TMEM.
+//   * The two query tiles ping-pong: while one warpgroup does its softmax the
+//     tensor core runs the other tile's products.
+//   * O is rescaled only when a row's running max grows by more than 2^8
+//     (P then stays <= 256, well inside fp16); the final O / l uses the same
+//     stale max for numerator and denominator, so the result is unchanged.
+//   * Causal: key tiles after a query tile's diagonal are never loaded or
+//     multiplied; only the diagonal tile is masked element-wise. CTAs are
+//     scheduled longest-first.
+//
+// TMEM columns (512 allocated): S_0 [0,128), S_1 [128,256), O_0 and O_1 after.
+// Every mbarrier wait is bounded; on timeout the CTA records the failure in
+// the device status word, drains its copies and MMAs, frees TMEM and exits.
+#include <cudaTypedefs.h>
+
+#include <mutex>
+
+#include "common.cuh"
+#include "launch.h"
+
+namespace fab {
+namespace {
+
+constexpr int kBM = 128;                   // query rows per tile (MMA M)
+constexpr int kBN = 128;                   // key rows per tile
+constexpr float kRescaleThreshold = 8.0f;  // log2 units: rescale O when m grows by > 2^8
+
+// Sites reported in the status word when a wait times out.
+enum : unsigned int {
+  kSiteLoadK = 101,
+  kSiteLoadV,
+  kSiteDrainLoads,
+  kSiteMmaQ,
+  kSiteMmaK,
+  kSiteMmaV,
+  kSiteMmaP,
+  kSiteDrainMma,
+  kSiteSoftS,
+  kSiteSoftO,
+  kSiteEpilogue
+};
+
+constexpr int pow2_ceil(int x) {
+  int p = 32;
+  while (p < x) p *= 2;
+  return p;
+}
+
+template <int D, int NQ>
+struct TcCfg {
+  static constexpr int KST = 2;                       // K stages
+  static constexpr int VST = 2;                       // V stages
+  static constexpr int NHALF = D / 64;                // 64-column swizzle blocks per row
+  static constexpr int BLK_BYTES = kBM * 64 * 2;      // one [128 rows][64 cols] block: 16 KB
+  static constexpr int TILE_BYTES = NHALF * BLK_BYTES;
+  static constexpr int Q_OFF = 0;
+  static constexpr int K_OFF = Q_OFF + NQ * TILE_BYTES;
+  static constexpr int V_OFF = K_OFF + KST * TILE_BYTES;
+  static constexpr int BAR_OFF = V_OFF + VST * TILE_BYTES;
+  static constexpr int NUM_BARS = 1 + 2 * KST + 2 * VST + 3 * NQ + 1;
+  static constexpr int MISC_OFF = BAR_OFF + NUM_BARS * 8;
+  static constexpr int SMEM_ALLOC = MISC_OFF + 16 + 1024;  // + slack to align the base to 1 KB
+  static constexpr int SOFT_WARPS = 4 * NQ;
+  static constexpr int MMA_WARP = SOFT_WARPS;
+  static constexpr int LOAD_WARP = SOFT_WARPS + 1;
+  static constexpr int THREADS = 32 * (SOFT_WARPS + 2);
+  static constexpr int O_COL = NQ * kBN;  // first O column; S_i at i * kBN
+  static constexpr int TMEM_COLS = pow2_ceil(NQ * (kBN + D));
+  static_assert(TMEM_COLS <= 512, "tensor memory holds 512 columns");
+  static_assert(SMEM_ALLOC <= 227 * 1024, "shared memory per CTA");
+};
+
+struct TcParams {
+  CUtensorMap tq, tk, tv;  // [bh][n][d] fp16, box 64 x 128 x 1, 128-byte swizzle
+  __half* o;
+  DeviceStatus* status;
+  unsigned long long timeout_ns;
+  int n;            // sequence length
+  int n_tiles;      // ceil(n / 128): query tiles = key tiles
+  int n_cta_tiles;  // ceil(n_tiles / NQ)
+  int causal;
+  float scale_log2;
+};
+
+__device__ __forceinline__ int kv_tiles_of(const TcParams& p, int qt) {
+  if (qt >= p.n_tiles) return 0;
+  return p.causal ? min(qt + 1, p.n_tiles) : p.n_tiles;
+}
+
+template <int D, int NQ>
+__global__ void __launch_bounds__(TcCfg<D, NQ>::THREADS, 1)
+    flash_tc_kernel(const __grid_constant__ TcParams p) {
+  using C = TcCfg<D, NQ>;
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* smem = reinterpret_cast<uint8_t*>(
+      (reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~static_cast<uintptr_t>(1023));
+  uint64_t* bars = reinterpret_cast<uint64_t*>(smem + C::BAR_OFF);
+  uint64_t* q_full = bars;
+  uint64_t* k_full = q_full + 1;
+  uint64_t* k_empty = k_full + C::KST;
+  uint64_t* v_full = k_empty + C::KST;
+  uint64_t* v_empty = v_full + C::VST;
+  uint64_t* s_full = v_empty + C::VST;  // MMA -> softmax: S_i ready
+  uint64_t* p_full = s_full + NQ;       // softmax -> MMA: P_i written (and O_i rescaled)
+  uint64_t* o_full = p_full + NQ;       // MMA -> softmax: O_i += P_i V done
+  uint64_t* drain = o_full + NQ;
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(smem + C::MISC_OFF);
+  volatile int* abort_flag = reinterpret_cast<volatile int*>(smem + C::MISC_OFF + 4);
+
+  const int warp = threadIdx.x >> 5;
+  const int lane = threadIdx.x & 31;
+  const int bh = blockIdx.x;
+  const int qt0 = (p.n_cta_tiles - 1 - static_cast<int>(blockIdx.y)) * NQ;  // longest first
+  const int nkv_max = kv_tiles_of(p, min(qt0 + NQ - 1, p.n_tiles - 1));
+
+  if (threadIdx.x == 0) {
+    mbar_init(q_full, 1);
+    for (int s = 0; s < C::KST; ++s) {
+      mbar_init(k_full + s, 1);
+      mbar_init(k_empty + s, 1);
+    }
+    for (int s = 0; s < C::VST; ++s) {
+      mbar_init(v_full + s, 1);
+      mbar_init(v_empty + s, 1);
+    }
+    for (int i = 0; i < NQ; ++i) {
+      mbar_init(s_full + i, 1);
+      mbar_init(p_full + i, 128);
+      mbar_init(o_full + i, 1);
+    }
+    mbar_init(drain, 1);
+    *abort_flag = 0;
+    fence_mbar_init();
+  }
+  if (warp == C::MMA_WARP) {
+    tmem_alloc(tmem_slot, C::TMEM_COLS);
+    tmem_relinquish();
+  }
+  if (warp == C::LOAD_WARP && lane == 0) {
+    prefetch_tensormap(&p.tq);
+    prefetch_tensormap(&p.tk);
+    prefetch_tensormap(&p.tv);
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem = *tmem_slot;
+
+  if (warp == C::LOAD_WARP) {
+    // ------------------------------------------------------------ TMA producer
+    if (lane == 0) {
+      int nq = 0;
+      for (int i = 0; i < NQ; ++i) nq += (qt0 + i < p.n_tiles) ? 1 : 0;
+      mbar_arrive_expect_tx(q_full, nq * C::TILE_BYTES);
+      for (int i = 0; i < nq; ++i)
+        for (int h = 0; h < C::NHALF; ++h)
+          tma_load_3d(smem + C::Q_OFF + i * C::TILE_BYTES + h * C::BLK_BYTES, &p.tq, q_full,
+                      h * 64, (qt0 + i) * kBM, bh);
+      int k_issued = 0, v_issued = 0;
+      for (int j = 0; j < nkv_max; ++j) {
+        const int ks = j % C::KST;
+        if (!mbar_wait(k_empty + ks, ((j / C::KST) & 1) ^ 1, abort_flag, p.status, kSiteLoadK,
+                       p.timeout_ns))
+          break;
+        mbar_arrive_expect_tx(k_full + ks, C::TILE_BYTES);
+        for (int h = 0; h < C::NHALF; ++h)
+          tma_load_3d(smem + C::K_OFF + ks * C::TILE_BYTES + h * C::BLK_BYTES, &p.tk,
+                      k_full + ks, h * 64, j * kBN, bh);
+        ++k_issued;
+        const int vs = j % C::VST;
+        if (!mbar_wait(v_empty + vs, ((j / C::VST) & 1) ^ 1, abort_flag, p.status, kSiteLoadV,
+                       p.timeout_ns))
+          break;
+        mbar_arrive_expect_tx(v_full + vs, C::TILE_BYTES);
+        for (int h = 0; h < C::NHALF; ++h)
+          tma_load_3d(smem + C::V_OFF + vs * C::TILE_BYTES + h * C::BLK_BYTES, &p.tv,
+                      v_full + vs, h * 64, j * kBN, bh);
+        ++v_issued;
+      }
+      // Never leave with a copy in flight: wait (bounded, regardless of the
+      // abort flag) for the last phase issued on every full barrier.
+      mbar_wait(q_full, 0, nullptr, p.status, kSiteDrainLoads, p.timeout_ns);
+      for (int s = 0; s < C::KST; ++s) {
+        const int cnt = k_issued > s ? (k_issued - 1 - s) / C::KST + 1 : 0;
+        if (cnt > 0)
+          mbar_wait(k_full + s, (cnt - 1) & 1, nullptr, p.status, kSiteDrainLoads, p.timeout_ns);
+      }
+      for (int s = 0; s < C::VST; ++s) {
+        const int cnt = v_issued > s ? (v_issued - 1 - s) / C::VST + 1 : 0;
+        if (cnt > 0)
+          mbar_wait(v_full + s, (cnt - 1) & 1, nullptr, p.status, kSiteDrainLoads, p.timeout_ns);
+      }
+    }
+  } else if (warp == C::MMA_WARP) {
+    // ------------------------------------------------------------- MMA issuer
+    if (lane == 0) {
+      constexpr uint32_t kIdescS = idesc_f16_f32(kBM, kBN, false, false);
+      constexpr uint32_t kIdescO = idesc_f16_f32(kBM, D, false, true);
+      const uint32_t q_base = smem_u32(smem + C::Q_OFF);
+      const uint32_t k_base = smem_u32(smem + C::K_OFF);
+      const uint32_t v_base = smem_u32(smem + C::V_OFF);
+      int nkv[NQ];
+#pragma unroll
+      for (int i = 0; i < NQ; ++i) nkv[i] = kv_tiles_of(p, qt0 + i);
+
+      // S_i = Q_i K^T: K = D in steps of 16 (32 bytes inside a 128-byte swizzle row).
+      auto issue_s = [&](int i, int ks) {
+        const uint32_t a0 = q_base + i * C::TILE_BYTES;
+        const uint32_t b0 = k_base + ks * C::TILE_BYTES;
+#pragma unroll
+        for (int kk = 0; kk < D / 16; ++kk) {
+          const uint32_t off = (kk >> 2) * C::BLK_BYTES + (kk & 3) * 32;
+          mma_f16_ss(tmem + i * kBN, sdesc_sw128(a0 + off, 16, 1024),
+                     sdesc_sw128(b0 + off, 16, 1024), kIdescS, kk > 0 ? 1u : 0u);
+        }
+      };
+      // O_i (+)= P_i V: K = 128 keys in steps of 16 rows (2 KB of V); V is
+      // MN-major, the 64-column blocks 16 KB apart (LBO), 8-row groups 1 KB (SBO).
+      auto issue_pv = [&](int i, int vs, bool accumulate) {
+        const uint32_t b0 = v_base + vs * C::TILE_BYTES;
+#pragma unroll
+        for (int kk = 0; kk < kBN / 16; ++kk) {
+          mma_f16_ts(tmem + C::O_COL + i * D, tmem + i * kBN + kk * 8,
+                     sdesc_sw128(b0 + kk * 2048, C::BLK_BYTES, 1024), kIdescO,
+                     (accumulate || kk > 0) ? 1u : 0u);
+        }
+      };
+
+      bool ok = mbar_wait(q_full, 0, abort_flag, p.status, kSiteMmaQ, p.timeout_ns) &&
+                mbar_wait(k_full, 0, abort_flag, p.status, kSiteMmaK, p.timeout_ns);
+      if (ok) {
+        tc_fence_after();
+#pragma unroll
+        for (int i = 0; i < NQ; ++i) {
+          if (nkv[i] > 0) {
+            issue_s(i, 0);
+            tc_commit(s_full + i);
+          }
+        }
+        tc_commit(k_empty);
+      }
+      for (int j = 0; ok && j < nkv_max; ++j) {
+        const int vs = j % C::VST;
+        ok = mbar_wait(v_full + vs, (j / C::VST) & 1, abort_flag, p.status, kSiteMmaV,
+                       p.timeout_ns);
+        if (!ok) break;
+        tc_fence_after();
+        const bool next = j + 1 < nkv_max;
+        const int ks = (j + 1) % C::KST;
+        bool k_ready = false;
+#pragma unroll
+        for (int i = 0; i < NQ; ++i) {
+          if (j < nkv[i]) {
+            ok = mbar_wait(p_full + i, j & 1, abort_flag, p.status, kSiteMmaP, p.timeout_ns);
+            if (!ok) break;
+            tc_fence_after();
+            issue_pv(i, vs, j > 0);
+            tc_commit(o_full + i);
+          }
+          if (next && j + 1 < nkv[i]) {
+            if (!k_ready) {
+              ok = mbar_wait(k_full + ks, ((j + 1) / C::KST) & 1, abort_flag, p.status, kSiteMmaK,
+                             p.timeout_ns);
+              if (!ok) break;
+              tc_fence_after();
+              k_ready = true;
+            }
+            issue_s(i, ks);
+            tc_commit(s_full + i);
+          }
+        }
+        if (!ok) break;
+        tc_commit(v_empty + vs);
+        if (next && k_ready) tc_commit(k_empty + ks);
+      }
+      // Every MMA issued completes before tensor memory is released.
+      tc_commit(drain);
+      mbar_wait(drain, 0, nullptr, p.status, kSiteDrainMma, p.timeout_ns);
+    }
+    __syncwarp();
+  } else {
+    // ------------------------------------------------------- softmax warpgroups
+    const int wg = warp >> 2;   // query tile of this warpgroup
+    const int quarter = warp & 3;  // TMEM lanes [32 quarter, 32 quarter + 32)
+    const int row = quarter * 32 + lane;
+    const int qt = qt0 + wg;
+    const int n_i = kv_tiles_of(p, qt);
+    if (n_i > 0) {
+      const uint32_t lane_off = static_cast<uint32_t>(quarter * 32) << 16;
+      const uint32_t t_s = tmem + lane_off + wg * kBN;
+      const uint32_t t_o = tmem + lane_off + C::O_COL + wg * D;
+      const int q_row = qt * kBM + row;
+      float m = -INFINITY;  // running max, log2 units
+      float l = 0.f;        // running sum of 2^(x - m)
+      bool ok = true;
+      for (int j = 0; j < n_i; ++j) {
+        ok = mbar_wait(s_full + wg, j & 1, abort_flag, p.status, kSiteSoftS, p.timeout_ns);
+        ok = __all_sync(0xffffffffu, ok);
+        if (!ok) break;
+        tc_fence_after();
+        // One register array for the row: fp32 scores in, packed fp16 P out
+        // (P pair c overwrites slot c, whose score was consumed at pair c / 2).
+        uint32_t sr[kBN];
+        tmem_ld128_wait(t_s, sr);
+#pragma unroll
+        for (int c = 0; c < kBN; ++c) sr[c] = __float_as_uint(__uint_as_float(sr[c]) * p.scale_log2);
+        const int k0 = j * kBN;
+        if ((p.causal && j == qt) || k0 + kBN > p.n) {
+          const int lim = p.causal ? min(q_row + 1, p.n) : p.n;  // keys [0, lim) are visible
+#pragma unroll
+          for (int c = 0; c < kBN; ++c)
+            if (k0 + c >= lim) sr[c] = __float_as_uint(-INFINITY);
+        }
+        float mt0 = __uint_as_float(sr[0]), mt1 = __uint_as_float(sr[1]);
+        float mt2 = __uint_as_float(sr[2]), mt3 = __uint_as_float(sr[3]);
+#pragma unroll
+        for (int c = 4; c < kBN; c += 4) {
+          mt0 = fmaxf(mt0, __uint_as_float(sr[c]));
+          mt1 = fmaxf(mt1, __uint_as_float(sr[c + 1]));
+          mt2 = fmaxf(mt2, __uint_as_float(sr[c + 2]));
+          mt3 = fmaxf(mt3, __uint_as_float(sr[c + 3]));
+        }
+        const float m_new = fmaxf(m, fmaxf(fmaxf(mt0, mt1), fmaxf(mt2, mt3)));
+        if (j == 0) {
+          m = m_new;
+        } else if (__any_sync(0xffffffffu, m_new > m + kRescaleThreshold)) {
+          // Rescale O to the new max; O_i must hold P_{j-1} V first.
+          const float alpha = fast_exp2(m - m_new);
+          ok = mbar_wait(o_full + wg, (j - 1) & 1, abort_flag, p.status, kSiteSoftO,
+                         p.timeout_ns);
+          ok = __all_sync(0xffffffffu, ok);
+          if (!ok) break;
+          tc_fence_after();
+#pragma unroll
+          for (int c0 = 0; c0 < D; c0 += 32) {
+            uint32_t o[32];
+            tmem_ld32_wait(t_o + c0, o);
+#pragma unroll
+            for (int e = 0; e < 32; ++e) o[e] = __float_as_uint(__uint_as_float(o[e]) * alpha);
+            tmem_st32<0>(t_o + c0, o);
+          }
+          tmem_st_wait();
+          l *= alpha;
+          m = m_new;
+        }
+        const float m_use = (m == -INFINITY) ? 0.f : m;
+        float rs0 = 0.f, rs1 = 0.f;
+#pragma unroll
+        for (int c = 0; c < kBN / 2; ++c) {
+          const float p0 = fast_exp2(__uint_as_float(sr[2 * c]) - m_use);
+          const float p1 = fast_exp2(__uint_as_float(sr[2 * c + 1]) - m_use);
+          rs0 += p0;
+          rs1 += p1;
+          sr[c] = pack_half2(p0, p1);
+        }
+        l += rs0 + rs1;
+        tmem_st32<0>(t_s, sr);
+        tmem_st32<32>(t_s + 32, sr);
+        tmem_st_wait();
+        tc_fence_before();
+        mbar_arrive(p_full + wg);
+      }
+      if (ok) {
+        ok = mbar_wait(o_full + wg, (n_i - 1) & 1, abort_flag, p.status, kSiteEpilogue,
+                       p.timeout_ns);
+        ok = __all_sync(0xffffffffu, ok);
+      }
+      if (ok) {
+        tc_fence_after();
+        const float inv = l > 0.f ? 1.f / l : 0.f;
+        __half* orow = p.o + (static_cast<size_t>(bh) * p.n + q_row) * D;
+#pragma unroll
+        for (int c0 = 0; c0 < D; c0 += 32) {
+          uint32_t o[32];
+          tmem_ld32_wait(t_o + c0, o);
+          uint32_t w[16];
+#pragma unroll
+          for (int e = 0; e < 16; ++e)
+            w[e] = pack_half2(__uint_as_float(o[2 * e]) * inv, __uint_as_float(o[2 * e + 1]) * inv);
+          if (q_row < p.n) {
+            uint4* dst = reinterpret_cast<uint4*>(orow + c0);
+#pragma unroll
+            for (int e = 0; e < 4; ++e)
+              dst[e] = make_uint4(w[4 * e], w[4 * e + 1], w[4 * e + 2], w[4 * e + 3]);
+          }
+        }
+      }
+    }
+  }
+
+  tc_fence_before();
+  __syncthreads();
+  if (warp == C::MMA_WARP) {
+    tc_fence_after();
+    tmem_dealloc(tmem, C::TMEM_COLS);
+  }
+}
+
+PFN_cuTensorMapEncodeTiled_v12000 tensor_map_encoder() {
+  static PFN_cuTensorMapEncodeTiled_v12000 fn = nullptr;
+  static std::once_flag once;
+  std::call_once(once, [] {
+    void* ptr = nullptr;
+    cudaDriverEntryPointQueryResult q;
+    if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &ptr, cudaEnableDefault, &q) ==
+            cudaSuccess &&
+        q == cudaDriverEntryPointSuccess)
+      fn = reinterpret_cast<PFN_cuTensorMapEncodeTiled_v12000>(ptr);
+  });
+  return fn;
+}
+
+// [bh][n][d] fp16 tensor, boxes of 64 columns x 128 rows, 128-byte swizzle.
+bool make_qkv_map(CUtensorMap* map, const void* base, int64_t bh, int64_t n, int d,
+                  std::string* err) {
+  auto encode = tensor_map_encoder();
+  if (encode == nullptr) {
+    *err = "cuTensorMapEncodeTiled is not available from the driver";
+    return false;
+  }
+  cuuint64_t dims[3] = {static_cast<cuuint64_t>(d), static_cast<cuuint64_t>(n),
+                        static_cast<cuuint64_t>(bh)};
+  cuuint64_t strides[2] = {static_cast<cuuint64_t>(d) * 2, static_cast<cuuint64_t>(n * d) * 2};
+  cuuint32_t box[3] = {64, 128, 1};
+  cuuint32_t estr[3] = {1, 1, 1};
+  CUresult r = encode(map, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 3, const_cast<void*>(base), dims,
+                      strides, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE,
+                      CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                      CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  if (r != CUDA_SUCCESS) {
+    *err = "cuTensorMapEncodeTiled failed with CUresult " + std::to_string(static_cast<int>(r));
+    return false;
+  }
+  return true;
+}
+
+template <int D, int NQ>
+cudaError_t launch_tc(const TcParams& prm, int64_t bh, const LaunchCtx& ctx) {
+  using C = TcCfg<D, NQ>;
+  auto kern = flash_tc_kernel<D, NQ>;
+  static std::once_flag once;
+  static cudaError_t attr_err = cudaSuccess;
+  std::call_once(once, [&] {
+    attr_err = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                    C::SMEM_ALLOC);
+  });
+  if (attr_err != cudaSuccess) return attr_err;
+  dim3 grid(static_cast<unsigned>(bh), static_cast<unsigned>(prm.n_cta_tiles));
+  kern<<<grid, C::THREADS, C::SMEM_ALLOC, ctx.stream>>>(prm);
+  return cudaGetLastError();
+}
+
+}  // namespace
+
+cudaError_t launch_flash_tc(const void* q, const void* k, const void* v, void* o, int64_t bh,
+                            int64_t n, int d, bool causal, float scale, const LaunchCtx& ctx,
+                            std::string* err) {
+  constexpr int kNQ = 2;
+  TcParams prm;
+  if (!make_qkv_map(&prm.tq, q, bh, n, d, err) || !make_qkv_map(&prm.tk, k, bh, n, d, err) ||
+      !make_qkv_map(&prm.tv, v, bh, n, d, err))
+    return cudaErrorInvalidValue;
+  prm.o = static_cast<__half*>(o);
+  prm.status = ctx.status;
+  prm.timeout_ns = ctx.timeout_ns;
+  prm.n = static_cast<int>(n);
+  prm.n_tiles = static_cast<int>((n + kBM - 1) / kBM);
+  prm.n_cta_tiles = (prm.n_tiles + kNQ - 1) / kNQ;
+  prm.causal = causal ? 1 : 0;
+  prm.scale_log2 = scale * kLog2e;
+  if (d == 64) return launch_tc<64, kNQ>(prm, bh, ctx);
+  return launch_tc<128, kNQ>(prm, bh, ctx);
+}
+
+}  // namespace fab
