@@ -209,3 +209,359 @@ def roofline(bound, work_per_launch, ms_per_launch, peaks, peak_src, traffic=Non
     return {"bound": bound, "achieved": round(achieved, 2), "peak": peak, "unit": unit,
             "frac": round(achieved / peak, 4), "traffic": traffic,
             "peak_source": f"{peak_src} ({'dense bf16/fp16 burst' if bound == 'tensor' else 'HBM copy'})"}
+
+
+# ----------------------------------------------------------------- workloads
+
+
+def randn_half(shape, gen, device, scale=1.0):
+    t = torch.randn(shape, generator=gen, device=device, dtype=torch.float32)
+    if scale != 1.0:
+        t.mul_(scale)
+    return t.half()
+
+
+def synthetic_paged_cache(ctx_lens, kv_heads, head_dim, block_size, seed, device):
+    """Seeded paged cache: block tables are one random permutation of the pool."""
+    g = torch.Generator().manual_seed(seed)
+    nblk = [-(-c // block_size) for c in ctx_lens]
+    pool = sum(nblk)
+    perm = torch.randperm(pool, generator=g).to(torch.int32)
+    tables = torch.zeros(len(ctx_lens), max(nblk), dtype=torch.int32)
+    pos = 0
+    for b, n in enumerate(nblk):
+        tables[b, :n] = perm[pos:pos + n]
+        pos += n
+    gd = torch.Generator(device=device).manual_seed(seed)
+    shape = (pool, kv_heads, block_size, head_dim)
+    kc = randn_half(shape, gd, device)
+    vc = randn_half(shape, gd, device)
+    return kc, vc, tables.to(device), torch.tensor(ctx_lens, dtype=torch.int32, device=device)
+
+
+def bench_prefill_cfg2(args, d: Dist, peaks, peak_src, traffic):
+    """Headline: config 2 per rank (weak scaling); kernel roofline; e2e with host buffers."""
+    import attnkernels as ak
+
+    c = CFG2
+    shape = (c["batch"], c["heads"], c["seq"], c["head_dim"])
+    gen = torch.Generator(device=d.device).manual_seed(1000 + d.rank)
+    q, k, v = (randn_half(shape, gen, d.device) for _ in range(3))
+    fn = lambda: ak.flash_attention(q, k, v, causal=True)  # noqa: E731
+    with ClockSampler(d.local) as clk:
+        ms = timed(fn, args.steps, args.warmup, d, spin_s=args.spin)
+    flops = prefill_flops(**c)
+    res = {
+        "ms_per_step": ms / args.steps,
+        "value": flops * d.world / (ms / args.steps * 1e-3) / 1e12,
+        "roofline": roofline("tensor", flops, ms / args.steps, peaks, peak_src,
+                             traffic.get("flash_tc_kernel_cfg2")),
+        "clocks": clk.summary(),
+        "gpu_launches": args.steps,  # one flash_tc_kernel launch per step
+    }
+    # End to end through the public API: pinned host q, k, v -> device, attention,
+    # output -> pinned host, every step.
+    hq, hk, hv = (t.cpu().pin_memory() for t in (q, k, v))
+    ho = torch.empty_like(hq).pin_memory()
+    del q, k, v
+    stream = torch.cuda.current_stream(d.device)
+
+    def e2e():
+        dq = hq.to(d.device, non_blocking=True)
+        dk = hk.to(d.device, non_blocking=True)
+        dv = hv.to(d.device, non_blocking=True)
+        ho.copy_(ak.flash_attention(dq, dk, dv, causal=True), non_blocking=True)
+
+    ms_e2e = timed(e2e, args.steps, args.warmup, d)
+    stream.synchronize()
+    res["e2e"] = {"value": round(flops * d.world / (ms_e2e / args.steps * 1e-3) / 1e12, 3),
+                  "unit": "TFLOP/s", "ms_per_step": round(ms_e2e / args.steps, 4),
+                  "h2d_bytes_per_step": 3 * hq.numel() * 2, "d2h_bytes_per_step": ho.numel() * 2}
+    return res
+
+
+def bench_decode_cfg4(args, d: Dist, peaks, peak_src, traffic):
+    """Config 4 per rank (independent sequences: weak scaling)."""
+    import attnkernels as ak
+
+    c = CFG4
+    g = torch.Generator().manual_seed(4000 + d.rank)
+    ctx = torch.randint(c["ctx_lo"], c["ctx_hi"] + 1, (c["batch"],), generator=g).tolist()
+    kc, vc, tables, lens = synthetic_paged_cache(ctx, c["kv_heads"], c["head_dim"],
+                                                 c["block_size"], 4000 + d.rank, d.device)
+    gq = torch.Generator(device=d.device).manual_seed(4100 + d.rank)
+    q = randn_half((c["batch"], c["heads"], 1, c["head_dim"]), gq, d.device)
+    max_ctx = max(ctx)
+    fn = lambda: ak.paged_decode(q, kc, vc, tables, lens, max_ctx,  # noqa: E731
+                                 partition_size=c["partition"])
+    with ClockSampler(d.local) as clk:
+        ms = timed(fn, args.steps, args.warmup, d, spin_s=args.spin)
+    nbytes = kv_bytes(ctx, c["kv_heads"], c["head_dim"])
+    res = {
+        "config": {"workload": "paged decode, BASELINE config 4", "batch": c["batch"],
+                   "heads": c["heads"], "kv_heads": c["kv_heads"], "head_dim": c["head_dim"],
+                   "block_size": c["block_size"], "ctx_mean": sum(ctx) / len(ctx),
+                   "ctx_max": max_ctx, "partition": c["partition"],
+                   "l2": "inputs larger than L2 (KV %.2f GB)" % (nbytes / 1e9)},
+        "metric": "paged-decode KV GB/s", "unit": "GB/s",
+        "ms_per_step": ms / args.steps,
+        "value": nbytes * d.world / (ms / args.steps * 1e-3) / 1e9,
+        # The timed op is memset + decode kernel + merge kernel: the kernel's own
+        # time is lower, so this fraction is a lower bound.
+        "roofline": roofline("hbm", nbytes, ms / args.steps, peaks, peak_src,
+                             traffic.get("paged_decode_kernel_cfg4")),
+        "clocks": clk.summary(),
+        "gpu_launches": 2 * args.steps,  # decode + merge kernels (plus one memset node)
+    }
+    hq = q.cpu().pin_memory()
+    htab, hlen = tables.cpu().pin_memory(), lens.cpu().pin_memory()
+    ho = torch.empty_like(hq).pin_memory()
+
+    def e2e():
+        dq = hq.to(d.device, non_blocking=True)
+        dt = htab.to(d.device, non_blocking=True)
+        dl = hlen.to(d.device, non_blocking=True)
+        ho.copy_(ak.paged_decode(dq, kc, vc, dt, dl, max_ctx, partition_size=c["partition"]),
+                 non_blocking=True)
+
+    ms_e2e = timed(e2e, args.steps, args.warmup, d)
+    res["e2e"] = {"value": round(nbytes * d.world / (ms_e2e / args.steps * 1e-3) / 1e9, 1),
+                  "unit": "GB/s", "ms_per_step": round(ms_e2e / args.steps, 4),
+                  "h2d_bytes_per_step": hq.numel() * 2 + htab.numel() * 4 + hlen.numel() * 4,
+                  "d2h_bytes_per_step": ho.numel() * 2,
+                  "note": "the KV cache is resident state; per step the query, block tables "
+                          "and lengths go up and the output comes back"}
+    return res
+
+
+def bench_long_context(args, d: Dist, peaks, peak_src):
+    """Configs 3 and 5, total work fixed and split over the ranks (strong scaling)."""
+    import attnkernels as ak
+    from attnkernels import parallel
+
+    out = {}
+    # Config 3: heads sharded, no collective.
+    c = CFG3
+    h0, h1 = parallel.head_range(c["heads"], d.world, d.rank)
+    gen = torch.Generator(device=d.device).manual_seed(3000 + h0)
+    shape = (c["batch"], h1 - h0, c["seq"], c["head_dim"])
+    q, k, v = (randn_half(shape, gen, d.device, c["input_scale"]) for _ in range(3))
+    ms = timed(lambda: ak.flash_attention(q, k, v, causal=True), args.steps, args.warmup, d)
+    flops = prefill_flops(**{x: c[x] for x in ("batch", "heads", "seq", "head_dim", "causal")})
+    per_rank = prefill_flops(c["batch"], h1 - h0, c["seq"], c["head_dim"], True)
+    out["config3_prefill"] = {
+        "workload": "causal prefill B=1 H=32 N=32768 d=128, heads sharded over ranks",
+        "heads_per_rank": h1 - h0, "scaling": "strong", "ms_per_step": round(ms / args.steps, 4),
+        "value": round(flops / (ms / args.steps * 1e-3) / 1e12, 2), "unit": "TFLOP/s",
+        "roofline": roofline("tensor", per_rank, ms / args.steps, peaks, peak_src),
+        "gpu_launches": args.steps}
+    del q, k, v
+    torch.cuda.empty_cache()
+
+    # Config 5: each sequence's context split into block-aligned ranges, one per
+    # rank; partials merged across ranks (one NCCL all-gather per step).
+    c = CFG5
+    t0, t1 = parallel.context_range(c["ctx"], c["block_size"], d.world, d.rank)
+    local = [t1 - t0] * c["batch"]
+    kc, vc, tables, lens = synthetic_paged_cache(local, c["kv_heads"], c["head_dim"],
+                                                 c["block_size"], 5000 + d.rank, d.device)
+    gq = torch.Generator(device=d.device).manual_seed(5100)  # the same q on every rank
+    q = randn_half((c["batch"], c["heads"], c["head_dim"]), gq, d.device)
+    part = ak.decode_partition(c["batch"], c["kv_heads"], t1 - t0)
+    if d.world == 1:
+        fn = lambda: ak.paged_decode(q, kc, vc, tables, lens, t1 - t0,  # noqa: E731
+                                     partition_size=part)
+        launches = 2
+    else:
+        cp = parallel.ContextParallelDecode()
+        fn = lambda: cp(q, kc, vc, tables, lens, t1 - t0, partition_size=part)  # noqa: E731
+        launches = 3
+    ms = timed(fn, args.steps, args.warmup, d)
+    total = kv_bytes([c["ctx"]] * c["batch"], c["kv_heads"], c["head_dim"])
+    out["config5_decode"] = {
+        "workload": "paged decode B=8 H=32 d=128 ctx=131072, context ranges over ranks, "
+                    "NCCL all-gather + merge of the (o, m, l) partials",
+        "tokens_per_rank": t1 - t0, "partition": part, "scaling": "strong",
+        "ms_per_step": round(ms / args.steps, 4),
+        "value": round(total / (ms / args.steps * 1e-3) / 1e9, 1), "unit": "GB/s",
+        "roofline": roofline("hbm", total / d.world, ms / args.steps, peaks, peak_src),
+        "gpu_launches": launches * args.steps}
+    return out
+
+
+def _timed_cpu(fn, min_s=10.0, max_reps=50):
+    fn()  # warm-up
+    reps, t0 = 0, time.perf_counter()
+    while True:
+        fn()
+        reps += 1
+        el = time.perf_counter() - t0
+        if (el >= min_s and reps >= 3) or reps >= max_reps:
+            return el, reps
+
+
+def cpu_baseline(min_s=10.0):
+    """The oracle (reference.py restated) on this host's cores, bounded samples."""
+    from oracle import reference as ref
+
+    torch.set_num_threads(os.cpu_count() or 1)
+    cores = torch.get_num_threads()
+    g = torch.Generator().manual_seed(7)
+    c = CFG2
+    q, k, v = (torch.randn(1, 1, c["seq"], c["head_dim"], generator=g).half() for _ in range(3))
+    el, reps = _timed_cpu(lambda: ref.attention_fp32(q, k, v, causal=True), min_s)
+    flops = prefill_flops(1, 1, c["seq"], c["head_dim"], True)
+    pre = {"value": round(flops * reps / el / 1e12, 5), "unit": "TFLOP/s", "cores": cores,
+           "kind": "port",
+           "sample": f"1 of 64 (batch, head) pairs of config 2 (N=4096, d=128, causal) per "
+                     f"call, {reps} calls in {el:.1f} s"}
+    c = CFG4
+    gen = torch.Generator().manual_seed(8)
+    ctx = torch.randint(c["ctx_lo"], c["ctx_hi"] + 1, (2,), generator=gen).tolist()
+    kc, vc, tables, lens = synthetic_paged_cache(ctx, c["kv_heads"], c["head_dim"],
+                                                 c["block_size"], 8, "cpu")
+    qd = torch.randn(2, c["heads"], c["head_dim"], generator=gen).half()
+    el, reps = _timed_cpu(lambda: ref.paged_decode_fp32(qd, kc, vc, tables, lens), min_s)
+    dec = {"value": round(kv_bytes(ctx, c["kv_heads"], c["head_dim"]) * reps / el / 1e9, 4),
+           "unit": "GB/s", "cores": cores, "kind": "port",
+           "sample": f"2 of 64 sequences of config 4 (ctx {ctx}), {reps} calls in {el:.1f} s"}
+    return pre, dec
+
+
+def reference_arm(args):
+    """The reference's CPU implementation (oracle port), K timed steps of a bounded sample."""
+    from oracle import reference as ref
+
+    torch.set_num_threads(os.cpu_count() or 1)
+    cores = torch.get_num_threads()
+    c = CFG2
+    g = torch.Generator().manual_seed(7)
+    q, k, v = (torch.randn(1, 1, c["seq"], c["head_dim"], generator=g).half() for _ in range(3))
+    step = lambda: ref.attention_fp32(q, k, v, causal=True)  # noqa: E731
+    for _ in range(args.warmup):
+        step()
+    t0 = time.perf_counter()
+    for _ in range(args.steps):
+        step()
+    el = time.perf_counter() - t0
+    flops = prefill_flops(1, 1, c["seq"], c["head_dim"], True)
+    value = flops * args.steps / el / 1e12
+    sample = ("each step: 1 of the 64 (batch, head) pairs of config 2 (B=4, H=16, N=4096, "
+              "d=128, causal), fp32 on the host cores")
+    return {
+        "impl": "reference", "metric": BASELINE_METRIC, "value": round(value, 5),
+        "unit": "TFLOP/s", "n_gpus": args.gpus, "steps": args.steps, "warmup": args.warmup,
+        "ms_per_step": round(el / args.steps * 1e3, 3), "higher_is_better": True,
+        "scaling": "weak", "vs_baseline": None, "dtype": "fp32", "data": "synthetic",
+        "config": {"workload": "causal prefill, BASELINE config 2 (bounded sample per step)",
+                   "batch": 1, "heads": 1, "seq_len": c["seq"], "head_dim": c["head_dim"],
+                   "causal": True},
+        "cpu_baseline": {"value": round(value, 5), "unit": "TFLOP/s", "cores": cores,
+                         "kind": "port", "sample": sample},
+        "e2e": {"value": round(value, 5), "unit": "TFLOP/s", "h2d_bytes_per_step": 0,
+                "d2h_bytes_per_step": 0},
+        "note": "oracle/reference.py restates the reference's attnkernels/reference.py "
+                "(its fp32 PyTorch path); the reference itself is Python and cannot travel "
+                "to this host",
+    }
+
+
+def profile_case(kind, d: Dist):
+    """One small case for an ncu capture: inputs above L2, a few GB at most."""
+    import attnkernels as ak
+
+    if kind == "prefill":
+        c = CFG2  # 192 MiB of q, k, v
+        gen = torch.Generator(device=d.device).manual_seed(1000)
+        shape = (c["batch"], c["heads"], c["seq"], c["head_dim"])
+        q, k, v = (randn_half(shape, gen, d.device) for _ in range(3))
+        fn = lambda: ak.flash_attention(q, k, v, causal=True)  # noqa: E731
+    else:
+        c = CFG4  # batch 16 of config 4: about 1.1 GB of K/V
+        g = torch.Generator().manual_seed(4000)
+        ctx = torch.randint(c["ctx_lo"], c["ctx_hi"] + 1, (16,), generator=g).tolist()
+        kc, vc, tables, lens = synthetic_paged_cache(ctx, c["kv_heads"], c["head_dim"],
+                                                     c["block_size"], 4000, d.device)
+        q = randn_half((16, c["heads"], c["head_dim"]),
+                       torch.Generator(device=d.device).manual_seed(1), d.device)
+        fn = lambda: ak.paged_decode(q, kc, vc, tables, lens, max(ctx),  # noqa: E731
+                                     partition_size=c["partition"])
+    for _ in range(5):
+        fn()
+    torch.cuda.synchronize(d.device)
+    ak.check_device_status(d.device)
+
+
+def main():
+    ap = argparse.ArgumentParser(description="attention hot paths on B200")
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=20)
+    ap.add_argument("--warmup", type=int, default=5)
+    ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
+    ap.add_argument("--no-long", action="store_true", help="skip configs 3 and 5")
+    ap.add_argument("--no-cpu", action="store_true", help="skip the CPU baseline")
+    ap.add_argument("--only-prefill", action="store_true", help="headline kernel only")
+    ap.add_argument("--spin", type=float, default=1.0,
+                    help="seconds of untimed load before a timed region (clock sampling)")
+    ap.add_argument("--profile", choices=["prefill", "decode"],
+                    help="run one small case of a kernel (3 + 2 launches) for ncu, no timing")
+    args = ap.parse_args()
+    if args.warmup < 3:
+        raise SystemExit("--warmup must be >= 3")
+
+    if args.impl == "reference":
+        if int(os.environ.get("RANK", "0")) != 0:
+            return
+        print(json.dumps(reference_arm(args)), flush=True)
+        return
+
+    d = Dist(args.gpus)
+    import attnkernels as ak
+
+    ak.load_extension()  # fails loudly without the native library
+    if args.profile:
+        profile_case(args.profile, d)
+        return
+    peaks, peak_src = load_peaks()
+    traffic = load_traffic()
+    pre = bench_prefill_cfg2(args, d, peaks, peak_src, traffic)
+    line = {
+        "metric": BASELINE_METRIC,
+        "value": round(pre["value"], 2),
+        "unit": "TFLOP/s",
+        "value_is": "causal prefill TFLOP/s, BASELINE config 2 per GPU, summed over GPUs",
+        "n_gpus": d.world, "steps": args.steps, "warmup": args.warmup,
+        "ms_per_step": round(pre["ms_per_step"], 4),
+        "higher_is_better": True, "scaling": "weak",
+        "vs_baseline": round(pre["value"] / d.world / 13.94, 2),
+        "vs_baseline_ref": "per GPU vs the reference's flash_wmma_bn32 on the same config on "
+                           "a T4, 13.94 TFLOP/s (BASELINE.md)",
+        "dtype": "fp16", "data": "synthetic",
+        "config": {"workload": "causal prefill, BASELINE config 2, one batch per GPU",
+                   "batch": CFG2["batch"], "heads": CFG2["heads"], "seq_len": CFG2["seq"],
+                   "head_dim": CFG2["head_dim"], "causal": True,
+                   "parallelism": f"{d.world} GPU(s), independent (batch, head) units, "
+                                  "no collective",
+                   "l2": "inputs larger than L2 (q, k, v 192 MiB per step), no flush"},
+        "roofline": pre["roofline"],
+        "e2e": pre["e2e"],
+        "gpu_launches": pre["gpu_launches"],
+        "clocks": pre["clocks"],
+    }
+    if not args.only_prefill:
+        line["decode"] = bench_decode_cfg4(args, d, peaks, peak_src, traffic)
+        if not args.no_long:
+            line["long_context"] = bench_long_context(args, d, peaks, peak_src)
+    ak.check_device_status(d.device)
+    if d.rank == 0 and d.world == 1 and not args.no_cpu:
+        pre_cpu, dec_cpu = cpu_baseline()
+        line["cpu_baseline"] = pre_cpu
+        if "decode" in line:
+            line["decode"]["cpu_baseline"] = dec_cpu
+    if d.rank == 0:
+        print(json.dumps(line), flush=True)
+    d.close()
+
+
+if __name__ == "__main__":
+    main()
