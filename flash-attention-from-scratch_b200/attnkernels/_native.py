@@ -44,6 +44,8 @@ SIGNATURES = {
                                           _i64, _i64, _i64, _i64, _i64, _f32, _i64, _vp, _size,
                                           _vp]),
     "attn_merge_partials": (_int, [_vp, _vp, _vp, _i64, _i64, _i64, _i64, _i64, _vp, _vp]),
+    "attn_paged_decode_noalloc": (_int, [_vp, _vp, _vp, _vp, _vp, _vp, _i64, _i64, _i64, _i64,
+                                         _i64, _i64, _i64, _i64, _f32, _i64, _vp]),
     "attn_device_status": (_int, [_u32p, _u32p]),
     "attn_selftest_wait_timeout": (_int, [ctypes.c_uint64, _vp]),
 }

@@ -323,4 +323,32 @@ int attn_selftest_wait_timeout(uint64_t timeout_ns, void* stream) {
   return ATTN_OK;
 }
 
+
+int attn_paged_decode_noalloc(const void* q, const void* k_cache, const void* v_cache,
+                              const int32_t* block_tables, const int32_t* context_lens, void* out,
+                              int64_t batch, int64_t num_heads, int64_t num_kv_heads,
+                              int64_t head_dim, int64_t block_size, int64_t num_blocks,
+                              int64_t max_blocks_per_seq, int64_t max_context_len, float scale,
+                              int64_t partition, void* stream) {
+  // Same argument checks as attn_paged_decode; the workspace fields are a
+  // stand-in here and are replaced by the library's fixed scratch array.
+  DecodeArgs a{q, k_cache, v_cache, block_tables, context_lens, out, nullptr, nullptr, nullptr,
+               batch, num_heads, num_kv_heads, head_dim, block_size, num_blocks,
+               max_blocks_per_seq, max_context_len, partition, scale,
+               reinterpret_cast<void*>(static_cast<uintptr_t>(256)), ~static_cast<size_t>(0)};
+  int rc = check_decode("paged_decode_noalloc", a);
+  if (rc != ATTN_OK) return rc;
+  if (out == nullptr || !aligned16(out))
+    return fail(ATTN_ERR_INVALID, "paged_decode_noalloc: out must be a 16-byte aligned pointer");
+  if (batch == 0) return ATTN_OK;
+  LaunchCtx ctx;
+  rc = device_ctx(static_cast<cudaStream_t>(stream), &ctx);
+  if (rc != ATTN_OK) return rc;
+  std::string err;
+  cudaError_t e = paged_decode_static_scratch(a, ctx, &err);
+  if (!err.empty()) return fail(ATTN_ERR_WORKSPACE, "%s", err.c_str());
+  if (e != cudaSuccess) return cuda_fail(e, "paged_decode_noalloc launch");
+  return ATTN_OK;
+}
+
 }  // extern "C"

@@ -640,4 +640,62 @@ cudaError_t launch_selftest_wait(unsigned long long timeout_ns, const LaunchCtx&
   return cudaGetLastError();
 }
 
+
+// ------------------------------------------------ allocation-free decode entry
+//
+// Some callers cannot allocate device memory at the point where they run decode:
+// a plugin inside a serving framework that owns the whole device-memory pool and
+// hands its plugins no allocator, or a latency-critical serving loop where a
+// cudaMalloc / cudaFree (which can synchronise the device) is not allowed. For
+// them the split-K scratch of the decode path (work counters and the fp32
+// (o, m, l) partials) can live in this fixed array instead of a caller
+// workspace. Every GPU that loads the library holds these bytes until the
+// process exits. All calls on a device share the array: calls that overlap on
+// the GPU (for example on two streams at once) race on it and must not be made.
+// The counters are cleared by every call; the partials are fully rewritten
+// before they are read.
+static __device__ __align__(256) uint8_t g_decode_scratch[kDecodeStaticScratchBytes];
+
+namespace {
+
+std::mutex g_scratch_mu;
+void* g_scratch_ptr[64] = {};
+
+}  // namespace
+
+cudaError_t paged_decode_static_scratch(DecodeArgs a, const LaunchCtx& ctx, std::string* err) {
+  const size_t need = decode_workspace_bytes(a.batch, a.hq, a.d, a.max_ctx, a.partition);
+  if (need > kDecodeStaticScratchBytes) {
+    *err = "paged_decode_noalloc: this problem needs " + std::to_string(need) +
+           " bytes of split-K scratch, above the fixed " +
+           std::to_string(kDecodeStaticScratchBytes) +
+           " bytes; use attn_paged_decode with a caller workspace, or a larger partition";
+    return cudaErrorInvalidValue;
+  }
+  int dev = 0;
+  cudaError_t e = cudaGetDevice(&dev);
+  if (e != cudaSuccess) return e;
+  if (dev < 0 || dev >= 64) return cudaErrorInvalidDevice;
+  void* base = nullptr;
+  {
+    // Set-up once per device, with that device current: the array's name is a
+    // host-side stand-in, so the kernels get its device address instead.
+    std::lock_guard<std::mutex> lock(g_scratch_mu);
+    if (g_scratch_ptr[dev] == nullptr) {
+      void* ptr = nullptr;
+      e = cudaGetSymbolAddress(&ptr, g_decode_scratch);
+      if (e != cudaSuccess) {
+        *err = std::string("paged_decode_noalloc: cudaGetSymbolAddress failed: ") +
+               cudaGetErrorString(e);
+        return e;
+      }
+      g_scratch_ptr[dev] = ptr;
+    }
+    base = g_scratch_ptr[dev];
+  }
+  a.workspace = base;
+  a.workspace_bytes = kDecodeStaticScratchBytes;
+  return launch_paged_decode(a, false, ctx);
+}
+
 }  // namespace fab

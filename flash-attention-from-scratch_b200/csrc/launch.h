@@ -62,4 +62,13 @@ cudaError_t launch_merge(const float* o_parts, const float* m_parts, const float
 
 cudaError_t launch_selftest_wait(unsigned long long timeout_ns, const LaunchCtx& ctx);
 
+// Size of the fixed device array that attn_paged_decode_noalloc uses as its
+// split-K scratch (32 MiB per device that loads the library).
+constexpr size_t kDecodeStaticScratchBytes = size_t(32) << 20;
+
+// paged_decode (final fp16 output) with the scratch in that fixed array; the
+// first call on a device looks up the array's device address. Fails with *err
+// set when the problem needs more scratch than the array holds.
+cudaError_t paged_decode_static_scratch(DecodeArgs a, const LaunchCtx& ctx, std::string* err);
+
 }  // namespace fab

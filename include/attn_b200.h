@@ -155,6 +155,32 @@ int attn_merge_partials(const float* o_parts, const float* m_parts, const float*
                         int64_t num_parts, int64_t rows, int64_t head_dim, int64_t o_part_stride,
                         int64_t ml_part_stride, void* out, void* stream);
 
+/*
+ * attn_paged_decode without a workspace argument, for callers that cannot
+ * allocate device memory where they run decode: a plugin inside a serving
+ * framework that owns the whole device-memory pool and gives its plugins no
+ * allocator, or a latency-critical loop in which cudaMalloc / cudaFree (which
+ * can synchronise the device) are not allowed. It calls no allocating routine.
+ * Its split-K scratch is a fixed 32 MiB (33554432-byte) array inside the
+ * library, which every GPU that loads the library holds until the process
+ * exits. Problems whose scratch, attn_paged_decode_workspace_bytes(batch,
+ * num_heads, head_dim, max_context_len, partition), exceeds 32 MiB are rejected
+ * with ATTN_ERR_WORKSPACE and a message; a larger partition shrinks the need.
+ * The first call on a device looks up the array's device address, so make it
+ * before any stream capture. All calls on a device share the array: calls that
+ * overlap on the GPU (two streams at once) race on it. Same arguments,
+ * checks and result as attn_paged_decode otherwise.
+ *
+ * No counterpart in the reference, whose paged_decode always allocates its
+ * scratch from the caching allocator.
+ */
+int attn_paged_decode_noalloc(const void* q, const void* k_cache, const void* v_cache,
+                              const int32_t* block_tables, const int32_t* context_lens, void* out,
+                              int64_t batch, int64_t num_heads, int64_t num_kv_heads,
+                              int64_t head_dim, int64_t block_size, int64_t num_blocks,
+                              int64_t max_blocks_per_seq, int64_t max_context_len, float scale,
+                              int64_t partition, void* stream);
+
 /* ------------------------------------------------------------ device status */
 
 /*
