@@ -142,6 +142,11 @@ __device__ __forceinline__ void prefetch_tensormap(const CUtensorMap* map) {
   asm volatile("prefetch.tensormap [%0];" ::"l"(reinterpret_cast<uint64_t>(map)) : "memory");
 }
 
+// Barrier `id` (1..15) over `threads` threads of the CTA.
+__device__ __forceinline__ void named_barrier_sync(int id, int threads) {
+  asm volatile("bar.sync %0, %1;" ::"r"(id), "r"(threads) : "memory");
+}
+
 // ------------------------------------------------------------------ tcgen05
 
 __device__ __forceinline__ void tmem_alloc(uint32_t* smem_result, uint32_t ncols) {
@@ -277,6 +282,71 @@ __device__ __forceinline__ float fast_exp2(float x) {
 __device__ __forceinline__ uint32_t pack_half2(float lo, float hi) {
   __half2 h = __floats2half2_rn(lo, hi);
   return *reinterpret_cast<uint32_t*>(&h);
+}
+
+// ---- packed fp32 pairs (sm_100 f32x2 arithmetic): lo in bits 0-31, hi in 32-63
+
+__device__ __forceinline__ uint64_t f2_pack(float lo, float hi) {
+  uint64_t r;
+  asm("mov.b64 %0, {%1, %2};" : "=l"(r) : "f"(lo), "f"(hi));
+  return r;
+}
+
+__device__ __forceinline__ void f2_unpack(uint64_t v, float& lo, float& hi) {
+  asm("mov.b64 {%0, %1}, %2;" : "=f"(lo), "=f"(hi) : "l"(v));
+}
+
+__device__ __forceinline__ uint64_t f2_fma(uint64_t a, uint64_t b, uint64_t c) {
+  uint64_t r;
+  asm("fma.rn.f32x2 %0, %1, %2, %3;" : "=l"(r) : "l"(a), "l"(b), "l"(c));
+  return r;
+}
+
+__device__ __forceinline__ uint64_t f2_add(uint64_t a, uint64_t b) {
+  uint64_t r;
+  asm("add.rn.f32x2 %0, %1, %2;" : "=l"(r) : "l"(a), "l"(b));
+  return r;
+}
+
+__device__ __forceinline__ uint64_t f2_mul(uint64_t a, uint64_t b) {
+  uint64_t r;
+  asm("mul.rn.f32x2 %0, %1, %2;" : "=l"(r) : "l"(a), "l"(b));
+  return r;
+}
+
+__device__ __forceinline__ float fmax3(float a, float b, float c) {
+  float r;
+  asm("max.f32 %0, %1, %2, %3;" : "=f"(r) : "f"(a), "f"(b), "f"(c));
+  return r;
+}
+
+// 2^x for a pair, on the FMA and integer pipes instead of the MUFU: Cody-Waite
+// range reduction x = n + f, n = round(x) (by adding and subtracting
+// 1.5 * 2^23), f in [-1/2, 1/2]; 2^f by a degree-3 polynomial with
+// minimax relative error 7.5e-5 on that interval (coefficients fitted for this
+// kernel by the Remez exchange); 2^n applied by adding n to the exponent
+// field. Inputs below -126 are clamped there (result < 2^-125, which becomes 0
+// in fp16); the attention kernel only evaluates x <= 8.
+__device__ __forceinline__ uint64_t f2_exp2_poly(uint64_t x) {
+  constexpr float kRound = 12582912.0f;  // 1.5 * 2^23
+  constexpr float c0 = 0.99992806f, c1 = 0.69326097f, c2 = 0.24261113f, c3 = 0.055171669f;
+  float xl, xh;
+  f2_unpack(x, xl, xh);
+  x = f2_pack(fmaxf(xl, -126.f), fmaxf(xh, -126.f));
+  const uint64_t t = f2_add(x, f2_pack(kRound, kRound));
+  const uint64_t nf = f2_add(t, f2_pack(-kRound, -kRound));
+  float nl, nh;
+  f2_unpack(nf, nl, nh);
+  const uint64_t f = f2_add(x, f2_pack(-nl, -nh));
+  uint64_t p = f2_fma(f2_pack(c3, c3), f, f2_pack(c2, c2));
+  p = f2_fma(p, f, f2_pack(c1, c1));
+  p = f2_fma(p, f, f2_pack(c0, c0));
+  float tl, th, pl, ph;
+  f2_unpack(t, tl, th);
+  f2_unpack(p, pl, ph);
+  const uint32_t rl = __float_as_uint(pl) + (__float_as_uint(tl) << 23);
+  const uint32_t rh = __float_as_uint(ph) + (__float_as_uint(th) << 23);
+  return f2_pack(__uint_as_float(rl), __uint_as_float(rh));
 }
 
 __device__ __forceinline__ float warp_max(float v) {

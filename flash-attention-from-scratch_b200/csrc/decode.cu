@@ -83,18 +83,6 @@ struct DecParams {
 };
 
 
-// 8 fp16 -> 8 fp32 from a 16-byte shared-memory load.
-__device__ __forceinline__ void load8_f32(const __half* src, float* dst) {
-  const uint4 raw = *reinterpret_cast<const uint4*>(src);
-  const __half2* h = reinterpret_cast<const __half2*>(&raw);
-#pragma unroll
-  for (int i = 0; i < 4; ++i) {
-    const float2 f = __half22float2(h[i]);
-    dst[2 * i] = f.x;
-    dst[2 * i + 1] = f.y;
-  }
-}
-
 template <int D, int G>
 __global__ void __launch_bounds__(kThreads, 1) paged_decode_kernel(const DecParams p) {
   using C = DecCfg<D, G>;
@@ -230,9 +218,19 @@ __global__ void __launch_bounds__(kThreads, 1) paged_decode_kernel(const DecPara
   };
 
   // ---------------------------------------------------------- consumer state
-  float qf[G][C::E];  // q * scale * log2(e): the 16 (or 8) elements this lane multiplies
+  // q * scale * log2(e) as packed fp32 pairs: the 16 (or 8) elements this lane
+  // multiplies in the score phase.
+  uint64_t qf[G][C::E / 2];
   float m[G], l[G];
-  float acc[G][C::DV];
+  // Output columns [lane * DV, lane * DV + DV) as DV / 2 packed pairs. With
+  // G <= 2 two accumulator sets (even / odd tokens) halve the FMA chains.
+  constexpr int NACC = G <= 2 ? 2 : 1;
+  uint64_t acc[NACC][G][C::DV / 2];
+
+  auto half2_pair = [](uint32_t h2) {
+    const float2 f = __half22float2(*reinterpret_cast<const __half2*>(&h2));
+    return f2_pack(f.x, f.y);
+  };
 
   auto consume = [&]() -> bool {
     const unsigned int slot = c_item % C::STAGES;
@@ -245,34 +243,53 @@ __global__ void __launch_bounds__(kThreads, 1) paged_decode_kernel(const DecPara
     const int nt = md.w & 31;
     if (md.w & 32) {
       const __half* qs = reinterpret_cast<const __half*>(st + 2 * C::KV);
+      const uint64_t sc = f2_pack(p.scale_log2, p.scale_log2);
 #pragma unroll
       for (int g = 0; g < G; ++g) {
 #pragma unroll
         for (int e8 = 0; e8 < C::E / 8; ++e8) {
-          load8_f32(qs + g * D + e8 * 64 + l8 * 8, &qf[g][e8 * 8]);
-#pragma unroll
-          for (int i = 0; i < 8; ++i) qf[g][e8 * 8 + i] *= p.scale_log2;
+          const uint4 raw = *reinterpret_cast<const uint4*>(qs + g * D + e8 * 64 + l8 * 8);
+          qf[g][e8 * 4 + 0] = f2_mul(half2_pair(raw.x), sc);
+          qf[g][e8 * 4 + 1] = f2_mul(half2_pair(raw.y), sc);
+          qf[g][e8 * 4 + 2] = f2_mul(half2_pair(raw.z), sc);
+          qf[g][e8 * 4 + 3] = f2_mul(half2_pair(raw.w), sc);
         }
         m[g] = -INFINITY;
         l[g] = 0.f;
 #pragma unroll
-        for (int j = 0; j < C::DV; ++j) acc[g][j] = 0.f;
+        for (int a = 0; a < NACC; ++a)
+#pragma unroll
+          for (int j = 0; j < C::DV / 2; ++j) acc[a][g][j] = f2_pack(0.f, 0.f);
       }
     }
-    // Scores: token 4 * step + grp, 8 lanes per token.
+    // Scores: token 4 * step + grp, 8 lanes per token, two FMA chains per head.
     float s[kTok / 4][G];
     const __half* kst = reinterpret_cast<const __half*>(st);
 #pragma unroll
     for (int step = 0; step < kTok / 4; ++step) {
       const int t = step * 4 + grp;
-      float kf[C::E];
+      uint64_t kf[C::E / 2];
 #pragma unroll
-      for (int e8 = 0; e8 < C::E / 8; ++e8) load8_f32(kst + t * D + e8 * 64 + l8 * 8, &kf[e8 * 8]);
+      for (int e8 = 0; e8 < C::E / 8; ++e8) {
+        const uint4 raw = *reinterpret_cast<const uint4*>(kst + t * D + e8 * 64 + l8 * 8);
+        kf[e8 * 4 + 0] = half2_pair(raw.x);
+        kf[e8 * 4 + 1] = half2_pair(raw.y);
+        kf[e8 * 4 + 2] = half2_pair(raw.z);
+        kf[e8 * 4 + 3] = half2_pair(raw.w);
+      }
 #pragma unroll
       for (int g = 0; g < G; ++g) {
-        float dot = 0.f;
+        uint64_t d0 = f2_mul(qf[g][0], kf[0]);
+        uint64_t d1 = f2_mul(qf[g][1], kf[1]);
 #pragma unroll
-        for (int e = 0; e < C::E; ++e) dot = fmaf(qf[g][e], kf[e], dot);
+        for (int e = 2; e < C::E / 2; e += 2) {
+          d0 = f2_fma(qf[g][e], kf[e], d0);
+          d1 = f2_fma(qf[g][e + 1], kf[e + 1], d1);
+        }
+        float a0, a1, b0, b1;
+        f2_unpack(d0, a0, a1);
+        f2_unpack(d1, b0, b1);
+        float dot = (a0 + a1) + (b0 + b1);
         dot += __shfl_xor_sync(0xffffffffu, dot, 4);
         dot += __shfl_xor_sync(0xffffffffu, dot, 2);
         dot += __shfl_xor_sync(0xffffffffu, dot, 1);
@@ -297,31 +314,41 @@ __global__ void __launch_bounds__(kThreads, 1) paged_decode_kernel(const DecPara
       ps += __shfl_xor_sync(0xffffffffu, ps, 16);
       l[g] = l[g] * alpha + ps;
       m[g] = mn;
+      const uint64_t al2 = f2_pack(alpha, alpha);
 #pragma unroll
-      for (int j = 0; j < C::DV; ++j) acc[g][j] *= alpha;
+      for (int a = 0; a < NACC; ++a)
+#pragma unroll
+        for (int j = 0; j < C::DV / 2; ++j) acc[a][g][j] = f2_mul(acc[a][g][j], al2);
     }
-    // P V: lane owns output columns [lane * DV, lane * DV + DV).
+    // P V: lane owns output columns [lane * DV, lane * DV + DV). A full stage
+    // runs branch-free; a partial one (the last of a unit) skips the missing
+    // tokens, whose shared-memory rows hold stale data.
     const __half* vst = reinterpret_cast<const __half*>(st + C::KV) + lane * C::DV;
-#pragma unroll
-    for (int t = 0; t < kTok; ++t) {
-      if (t < nt) {
-        float vf[C::DV];
-        if constexpr (C::DV == 4) {
-          const uint2 raw = *reinterpret_cast<const uint2*>(vst + t * D);
-          const float2 a = __half22float2(*reinterpret_cast<const __half2*>(&raw.x));
-          const float2 b = __half22float2(*reinterpret_cast<const __half2*>(&raw.y));
-          vf[0] = a.x; vf[1] = a.y; vf[2] = b.x; vf[3] = b.y;
-        } else {
-          const float2 a = __half22float2(*reinterpret_cast<const __half2*>(vst + t * D));
-          vf[0] = a.x; vf[1] = a.y;
-        }
-#pragma unroll
-        for (int g = 0; g < G; ++g) {
-          const float pt = __shfl_sync(0xffffffffu, s[t >> 2][g], (t & 3) * 8);
-#pragma unroll
-          for (int j = 0; j < C::DV; ++j) acc[g][j] = fmaf(pt, vf[j], acc[g][j]);
-        }
+    auto pv = [&](int t) {
+      uint64_t vf[C::DV / 2];
+      if constexpr (C::DV == 4) {
+        const uint2 raw = *reinterpret_cast<const uint2*>(vst + t * D);
+        vf[0] = half2_pair(raw.x);
+        vf[1] = half2_pair(raw.y);
+      } else {
+        vf[0] = half2_pair(*reinterpret_cast<const uint32_t*>(vst + t * D));
       }
+#pragma unroll
+      for (int g = 0; g < G; ++g) {
+        const float pt = __shfl_sync(0xffffffffu, s[t >> 2][g], (t & 3) * 8);
+        const uint64_t pt2 = f2_pack(pt, pt);
+#pragma unroll
+        for (int j = 0; j < C::DV / 2; ++j)
+          acc[t % NACC][g][j] = f2_fma(pt2, vf[j], acc[t % NACC][g][j]);
+      }
+    };
+    if (nt == kTok) {
+#pragma unroll
+      for (int t = 0; t < kTok; ++t) pv(t);
+    } else {
+#pragma unroll
+      for (int t = 0; t < kTok; ++t)
+        if (t < nt) pv(t);
     }
     __syncwarp();
     if (md.w & 64) {
@@ -330,23 +357,31 @@ __global__ void __launch_bounds__(kThreads, 1) paged_decode_kernel(const DecPara
 #pragma unroll
       for (int g = 0; g < G; ++g) {
         const float inv = 1.f / l[g];
+        float o[C::DV];
+#pragma unroll
+        for (int j = 0; j < C::DV / 2; ++j) {
+          uint64_t v = acc[0][g][j];
+          if constexpr (NACC == 2) v = f2_add(v, acc[1][g][j]);
+          f2_unpack(v, o[2 * j], o[2 * j + 1]);
+          o[2 * j] *= inv;
+          o[2 * j + 1] *= inv;
+        }
         const size_t row = static_cast<size_t>(b) * p.hq + kvh * G + g;
         if (p.direct_out && ns == 1) {
           __half* dst = p.out + row * D + lane * C::DV;
           if constexpr (C::DV == 4) {
-            *reinterpret_cast<uint2*>(dst) = make_uint2(pack_half2(acc[g][0] * inv, acc[g][1] * inv),
-                                                        pack_half2(acc[g][2] * inv, acc[g][3] * inv));
+            *reinterpret_cast<uint2*>(dst) =
+                make_uint2(pack_half2(o[0], o[1]), pack_half2(o[2], o[3]));
           } else {
-            *reinterpret_cast<uint32_t*>(dst) = pack_half2(acc[g][0] * inv, acc[g][1] * inv);
+            *reinterpret_cast<uint32_t*>(dst) = pack_half2(o[0], o[1]);
           }
         } else {
           const size_t pr = row * p.num_splits + split;
           float* dst = p.o_part + pr * D + lane * C::DV;
           if constexpr (C::DV == 4) {
-            *reinterpret_cast<float4*>(dst) =
-                make_float4(acc[g][0] * inv, acc[g][1] * inv, acc[g][2] * inv, acc[g][3] * inv);
+            *reinterpret_cast<float4*>(dst) = make_float4(o[0], o[1], o[2], o[3]);
           } else {
-            *reinterpret_cast<float2*>(dst) = make_float2(acc[g][0] * inv, acc[g][1] * inv);
+            *reinterpret_cast<float2*>(dst) = make_float2(o[0], o[1]);
           }
           if (lane == 0) {
             p.m_part[pr] = m[g];

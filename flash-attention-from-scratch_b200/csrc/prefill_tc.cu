@@ -12,6 +12,9 @@
 //       warps 0-3, 4-7  softmax warpgroups, one per query tile, one thread per row
 //       warp  8         MMA issuer (one thread) + tensor-memory allocator
 //       warp  9         TMA producer (one thread)
+//       warps 10-11     idle (they complete the control warpgroup)
+//     setmaxnreg moves registers from the control warpgroup to the softmax
+//     warpgroups, so a whole 128-column score row stays in registers.
 //   * Q, K, V tiles arrive by TMA (128-byte swizzle, zero fill past the end of
 //     the sequence) into a 2-stage K ring and a 2-stage V ring.
 //   * S_i = Q_i K^T is a tcgen05.mma with both operands in shared memory and the
@@ -44,6 +47,13 @@ namespace {
 constexpr int kBM = 128;                   // query rows per tile (MMA M)
 constexpr int kBN = 128;                   // key rows per tile
 constexpr float kRescaleThreshold = 8.0f;  // log2 units: rescale O when m grows by > 2^8
+// Of the 128 exponentials per row, how many run on the FMA pipe (a compile-time
+// tuning constant; the rest use the MUFU).
+#ifndef FAB_POLY_COLS
+#define FAB_POLY_COLS 32
+#endif
+constexpr int kPolyCols = FAB_POLY_COLS;
+static_assert(kPolyCols % 2 == 0 && kPolyCols <= kBN, "pairs of columns");
 
 // Sites reported in the status word when a wait times out.
 enum : unsigned int {
@@ -81,9 +91,17 @@ struct TcCfg {
   static constexpr int MISC_OFF = BAR_OFF + NUM_BARS * 8;
   static constexpr int SMEM_ALLOC = MISC_OFF + 16 + 1024;  // + slack to align the base to 1 KB
   static constexpr int SOFT_WARPS = 4 * NQ;
-  static constexpr int MMA_WARP = SOFT_WARPS;
+  static constexpr int MMA_WARP = SOFT_WARPS;       // first warp of the control warpgroup
   static constexpr int LOAD_WARP = SOFT_WARPS + 1;
-  static constexpr int THREADS = 32 * (SOFT_WARPS + 2);
+  static constexpr int THREADS = 32 * (SOFT_WARPS + 4);
+  // Register split (setmaxnreg): launched at 168 per thread (65536 / 384,
+  // rounded down to 8); the control warpgroup drops to 56 and the softmax
+  // warpgroups rise to 224: 128 * 56 + 256 * 224 = 384 * 168.
+  static constexpr int LAUNCH_REGS = 168;
+  static constexpr int CONTROL_REGS = 56;
+  static constexpr int SOFTMAX_REGS = 224;
+  static_assert(NQ == 2, "the register split assumes two softmax warpgroups");
+  static_assert(128 * CONTROL_REGS + 256 * SOFTMAX_REGS <= THREADS * LAUNCH_REGS, "register split");
   static constexpr int O_COL = NQ * kBN;  // first O column; S_i at i * kBN
   static constexpr int TMEM_COLS = pow2_ceil(NQ * (kBN + D));
   static_assert(TMEM_COLS <= 512, "tensor memory holds 512 columns");
@@ -166,7 +184,11 @@ __global__ void __launch_bounds__(TcCfg<D, NQ>::THREADS, 1)
   tc_fence_after();
   const uint32_t tmem = *tmem_slot;
 
-  if (warp == C::LOAD_WARP) {
+  // Each role sets its register budget and ends at its own copy of the final
+  // barrier, so ptxas allocates every role's code at that role's budget.
+  if (warp >= C::SOFT_WARPS) {
+    asm volatile("setmaxnreg.dec.sync.aligned.u32 %0;" ::"n"(C::CONTROL_REGS));
+    if (warp == C::LOAD_WARP) {
     // ------------------------------------------------------------ TMA producer
     if (lane == 0) {
       int nq = 0;
@@ -298,8 +320,16 @@ __global__ void __launch_bounds__(TcCfg<D, NQ>::THREADS, 1)
       mbar_wait(drain, 0, nullptr, p.status, kSiteDrainMma, p.timeout_ns);
     }
     __syncwarp();
+    }
+    tc_fence_before();
+    named_barrier_sync(1, C::THREADS);
+    if (warp == C::MMA_WARP) {
+      tc_fence_after();
+      tmem_dealloc(tmem, C::TMEM_COLS);
+    }
   } else {
     // ------------------------------------------------------- softmax warpgroups
+    asm volatile("setmaxnreg.inc.sync.aligned.u32 %0;" ::"n"(C::SOFTMAX_REGS));
     const int wg = warp >> 2;   // query tile of this warpgroup
     const int quarter = warp & 3;  // TMEM lanes [32 quarter, 32 quarter + 32)
     const int row = quarter * 32 + lane;
@@ -320,10 +350,23 @@ __global__ void __launch_bounds__(TcCfg<D, NQ>::THREADS, 1)
         tc_fence_after();
         // One register array for the row: fp32 scores in, packed fp16 P out
         // (P pair c overwrites slot c, whose score was consumed at pair c / 2).
+        // With a positive scale the max is taken on the raw scores and the
+        // scale is folded into the exponent's FMA; otherwise the row is
+        // scaled first.
         uint32_t sr[kBN];
         tmem_ld128_wait(t_s, sr);
+        float cs = p.scale_log2;
+        if (cs <= 0.f) {
 #pragma unroll
-        for (int c = 0; c < kBN; ++c) sr[c] = __float_as_uint(__uint_as_float(sr[c]) * p.scale_log2);
+          for (int c = 0; c < kBN; c += 2) {
+            float a, b;
+            f2_unpack(f2_mul(f2_pack(__uint_as_float(sr[c]), __uint_as_float(sr[c + 1])),
+                             f2_pack(cs, cs)), a, b);
+            sr[c] = __float_as_uint(a);
+            sr[c + 1] = __float_as_uint(b);
+          }
+          cs = 1.f;
+        }
         const int k0 = j * kBN;
         if ((p.causal && j == qt) || k0 + kBN > p.n) {
           const int lim = p.causal ? min(q_row + 1, p.n) : p.n;  // keys [0, lim) are visible
@@ -331,16 +374,20 @@ __global__ void __launch_bounds__(TcCfg<D, NQ>::THREADS, 1)
           for (int c = 0; c < kBN; ++c)
             if (k0 + c >= lim) sr[c] = __float_as_uint(-INFINITY);
         }
-        float mt0 = __uint_as_float(sr[0]), mt1 = __uint_as_float(sr[1]);
-        float mt2 = __uint_as_float(sr[2]), mt3 = __uint_as_float(sr[3]);
+        float mt0 = fmax3(__uint_as_float(sr[0]), __uint_as_float(sr[1]), __uint_as_float(sr[2]));
+        float mt1 = fmax3(__uint_as_float(sr[3]), __uint_as_float(sr[4]), __uint_as_float(sr[5]));
+        float mt2 = fmax3(__uint_as_float(sr[6]), __uint_as_float(sr[7]), __uint_as_float(sr[8]));
+        float mt3 = fmax3(__uint_as_float(sr[9]), __uint_as_float(sr[10]), __uint_as_float(sr[11]));
 #pragma unroll
-        for (int c = 4; c < kBN; c += 4) {
-          mt0 = fmaxf(mt0, __uint_as_float(sr[c]));
-          mt1 = fmaxf(mt1, __uint_as_float(sr[c + 1]));
-          mt2 = fmaxf(mt2, __uint_as_float(sr[c + 2]));
-          mt3 = fmaxf(mt3, __uint_as_float(sr[c + 3]));
+        for (int c = 12; c + 8 <= kBN; c += 8) {
+          mt0 = fmax3(mt0, __uint_as_float(sr[c]), __uint_as_float(sr[c + 1]));
+          mt1 = fmax3(mt1, __uint_as_float(sr[c + 2]), __uint_as_float(sr[c + 3]));
+          mt2 = fmax3(mt2, __uint_as_float(sr[c + 4]), __uint_as_float(sr[c + 5]));
+          mt3 = fmax3(mt3, __uint_as_float(sr[c + 6]), __uint_as_float(sr[c + 7]));
         }
-        const float m_new = fmaxf(m, fmaxf(fmaxf(mt0, mt1), fmaxf(mt2, mt3)));
+        mt0 = fmax3(mt0, __uint_as_float(sr[kBN - 4]), __uint_as_float(sr[kBN - 3]));
+        mt1 = fmax3(mt1, __uint_as_float(sr[kBN - 2]), __uint_as_float(sr[kBN - 1]));
+        const float m_new = fmaxf(m, fmax3(mt0, mt1, fmaxf(mt2, mt3)) * cs);
         if (j == 0) {
           m = m_new;
         } else if (__any_sync(0xffffffffu, m_new > m + kRescaleThreshold)) {
@@ -356,24 +403,48 @@ __global__ void __launch_bounds__(TcCfg<D, NQ>::THREADS, 1)
             uint32_t o[32];
             tmem_ld32_wait(t_o + c0, o);
 #pragma unroll
-            for (int e = 0; e < 32; ++e) o[e] = __float_as_uint(__uint_as_float(o[e]) * alpha);
+            for (int e = 0; e < 32; e += 2) {
+              float a, b;
+              f2_unpack(f2_mul(f2_pack(__uint_as_float(o[e]), __uint_as_float(o[e + 1])),
+                               f2_pack(alpha, alpha)), a, b);
+              o[e] = __float_as_uint(a);
+              o[e + 1] = __float_as_uint(b);
+            }
             tmem_st32<0>(t_o + c0, o);
           }
           tmem_st_wait();
           l *= alpha;
           m = m_new;
         }
+        // P = 2^(cs * s - m): packed FMAs; the first columns on the MUFU, the
+        // last kPolyCols on the FMA pipe (f2_exp2_poly), to share the load.
         const float m_use = (m == -INFINITY) ? 0.f : m;
-        float rs0 = 0.f, rs1 = 0.f;
+        const uint64_t cs2 = f2_pack(cs, cs);
+        const uint64_t nm2 = f2_pack(-m_use, -m_use);
+        uint64_t rs0 = f2_pack(0.f, 0.f), rs1 = rs0;
 #pragma unroll
         for (int c = 0; c < kBN / 2; ++c) {
-          const float p0 = fast_exp2(__uint_as_float(sr[2 * c]) - m_use);
-          const float p1 = fast_exp2(__uint_as_float(sr[2 * c + 1]) - m_use);
-          rs0 += p0;
-          rs1 += p1;
-          sr[c] = pack_half2(p0, p1);
+          const uint64_t x =
+              f2_fma(f2_pack(__uint_as_float(sr[2 * c]), __uint_as_float(sr[2 * c + 1])), cs2, nm2);
+          uint64_t pr;
+          if (2 * c < kBN - kPolyCols) {
+            float a, b;
+            f2_unpack(x, a, b);
+            pr = f2_pack(fast_exp2(a), fast_exp2(b));
+          } else {
+            pr = f2_exp2_poly(x);
+          }
+          if (c & 1) rs1 = f2_add(rs1, pr); else rs0 = f2_add(rs0, pr);
+          float a, b;
+          f2_unpack(pr, a, b);
+          sr[c] = pack_half2(a, b);
         }
-        l += rs0 + rs1;
+        {
+          float a, b, c2, d2;
+          f2_unpack(rs0, a, b);
+          f2_unpack(rs1, c2, d2);
+          l += (a + b) + (c2 + d2);
+        }
         tmem_st32<0>(t_s, sr);
         tmem_st32<32>(t_s + 32, sr);
         tmem_st_wait();
@@ -406,13 +477,8 @@ __global__ void __launch_bounds__(TcCfg<D, NQ>::THREADS, 1)
         }
       }
     }
-  }
-
-  tc_fence_before();
-  __syncthreads();
-  if (warp == C::MMA_WARP) {
-    tc_fence_after();
-    tmem_dealloc(tmem, C::TMEM_COLS);
+    tc_fence_before();
+    named_barrier_sync(1, C::THREADS);
   }
 }
 
