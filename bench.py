@@ -389,7 +389,7 @@ def bench_long_context(args, d: Dist, peaks, peak_src):
     return out
 
 
-def _timed_cpu(fn, min_s=10.0, max_reps=50):
+def _timed_cpu(fn, min_s=10.0, max_reps=100000):
     fn()  # warm-up
     reps, t0 = 0, time.perf_counter()
     while True:

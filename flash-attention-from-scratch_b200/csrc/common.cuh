@@ -278,6 +278,13 @@ __device__ __forceinline__ float fast_exp2(float x) {
   return y;
 }
 
+// 2^x for both halves of a packed fp16x2 (hardware approximation).
+__device__ __forceinline__ uint32_t fast_exp2_h2(uint32_t x) {
+  uint32_t y;
+  asm("ex2.approx.f16x2 %0, %1;" : "=r"(y) : "r"(x));
+  return y;
+}
+
 // Two floats -> packed fp16x2 (lo in bits 0-15), round to nearest.
 __device__ __forceinline__ uint32_t pack_half2(float lo, float hi) {
   __half2 h = __floats2half2_rn(lo, hi);
@@ -326,27 +333,41 @@ __device__ __forceinline__ float fmax3(float a, float b, float c) {
 // minimax relative error 7.5e-5 on that interval (coefficients fitted for this
 // kernel by the Remez exchange); 2^n applied by adding n to the exponent
 // field. Inputs below -126 are clamped there (result < 2^-125, which becomes 0
-// in fp16); the attention kernel only evaluates x <= 8.
+// in fp16); the attention kernel only evaluates x <= 8. Written as one PTX
+// block so that it stays at about ten instructions per pair.
 __device__ __forceinline__ uint64_t f2_exp2_poly(uint64_t x) {
-  constexpr float kRound = 12582912.0f;  // 1.5 * 2^23
-  constexpr float c0 = 0.99992806f, c1 = 0.69326097f, c2 = 0.24261113f, c3 = 0.055171669f;
-  float xl, xh;
-  f2_unpack(x, xl, xh);
-  x = f2_pack(fmaxf(xl, -126.f), fmaxf(xh, -126.f));
-  const uint64_t t = f2_add(x, f2_pack(kRound, kRound));
-  const uint64_t nf = f2_add(t, f2_pack(-kRound, -kRound));
-  float nl, nh;
-  f2_unpack(nf, nl, nh);
-  const uint64_t f = f2_add(x, f2_pack(-nl, -nh));
-  uint64_t p = f2_fma(f2_pack(c3, c3), f, f2_pack(c2, c2));
-  p = f2_fma(p, f, f2_pack(c1, c1));
-  p = f2_fma(p, f, f2_pack(c0, c0));
-  float tl, th, pl, ph;
-  f2_unpack(t, tl, th);
-  f2_unpack(p, pl, ph);
-  const uint32_t rl = __float_as_uint(pl) + (__float_as_uint(tl) << 23);
-  const uint32_t rh = __float_as_uint(ph) + (__float_as_uint(th) << 23);
-  return f2_pack(__uint_as_float(rl), __uint_as_float(rh));
+  uint64_t r;
+  asm("{\n\t"
+      ".reg .f32 xl, xh;\n\t"
+      ".reg .b32 tl, th, pl, ph;\n\t"
+      ".reg .b64 xx, t, nf, f, p, rnd, nrnd, c0, c1, c2, c3;\n\t"
+      "mov.b64 {xl, xh}, %1;\n\t"
+      "max.f32 xl, xl, 0fC2FC0000;\n\t"   // -126
+      "max.f32 xh, xh, 0fC2FC0000;\n\t"
+      "mov.b64 xx, {xl, xh};\n\t"
+      "mov.b64 rnd, 0x4B4000004B400000;\n\t"   // 1.5 * 2^23 (both halves)
+      "mov.b64 nrnd, 0xCB400000CB400000;\n\t"
+      "mov.b64 c3, 0x3D61FBB03D61FBB0;\n\t"    // 0.055171669
+      "mov.b64 c2, 0x3E786F0D3E786F0D;\n\t"    // 0.24261113
+      "mov.b64 c1, 0x3F31798D3F31798D;\n\t"    // 0.69326097
+      "mov.b64 c0, 0x3F7FFB493F7FFB49;\n\t"    // 0.99992806
+      "add.rn.f32x2 t, xx, rnd;\n\t"
+      "add.rn.f32x2 nf, t, nrnd;\n\t"
+      "sub.rn.f32x2 f, xx, nf;\n\t"
+      "fma.rn.f32x2 p, c3, f, c2;\n\t"
+      "fma.rn.f32x2 p, p, f, c1;\n\t"
+      "fma.rn.f32x2 p, p, f, c0;\n\t"
+      "mov.b64 {tl, th}, t;\n\t"
+      "mov.b64 {pl, ph}, p;\n\t"
+      "shl.b32 tl, tl, 23;\n\t"
+      "shl.b32 th, th, 23;\n\t"
+      "add.s32 pl, pl, tl;\n\t"
+      "add.s32 ph, ph, th;\n\t"
+      "mov.b64 %0, {pl, ph};\n\t"
+      "}"
+      : "=l"(r)
+      : "l"(x));
+  return r;
 }
 
 __device__ __forceinline__ float warp_max(float v) {

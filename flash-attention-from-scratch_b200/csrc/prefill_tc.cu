@@ -16,7 +16,7 @@
 //     setmaxnreg moves registers from the control warpgroup to the softmax
 //     warpgroups, so a whole 128-column score row stays in registers.
 //   * Q, K, V tiles arrive by TMA (128-byte swizzle, zero fill past the end of
-//     the sequence) into a 2-stage K ring and a 2-stage V ring.
+//     the sequence) into one ring of K and V tiles (5 slots at D = 128).
 //   * S_i = Q_i K^T is a tcgen05.mma with both operands in shared memory and the
 //     fp32 result in tensor memory (TMEM). The softmax thread of row r reads row
 //     r of S_i from TMEM lane r, writes P as packed fp16 back over the first 64
@@ -50,9 +50,14 @@ constexpr float kRescaleThreshold = 8.0f;  // log2 units: rescale O when m grows
 // Of the 128 exponentials per row, how many run on the FMA pipe (a compile-time
 // tuning constant; the rest use the MUFU).
 #ifndef FAB_POLY_COLS
-#define FAB_POLY_COLS 32
+#define FAB_POLY_COLS 16
 #endif
 constexpr int kPolyCols = FAB_POLY_COLS;
+// 1: exponentials as ex2.approx.f16x2 (two per MUFU op); 0: fp32 ex2 (+ polynomial).
+#ifndef FAB_EXP_HALF2
+#define FAB_EXP_HALF2 0
+#endif
+constexpr bool kExpHalf2 = FAB_EXP_HALF2 != 0;
 static_assert(kPolyCols % 2 == 0 && kPolyCols <= kBN, "pairs of columns");
 
 // Sites reported in the status word when a wait times out.
@@ -78,16 +83,18 @@ constexpr int pow2_ceil(int x) {
 
 template <int D, int NQ>
 struct TcCfg {
-  static constexpr int KST = 2;                       // K stages
-  static constexpr int VST = 2;                       // V stages
   static constexpr int NHALF = D / 64;                // 64-column swizzle blocks per row
   static constexpr int BLK_BYTES = kBM * 64 * 2;      // one [128 rows][64 cols] block: 16 KB
   static constexpr int TILE_BYTES = NHALF * BLK_BYTES;
   static constexpr int Q_OFF = 0;
-  static constexpr int K_OFF = Q_OFF + NQ * TILE_BYTES;
-  static constexpr int V_OFF = K_OFF + KST * TILE_BYTES;
-  static constexpr int BAR_OFF = V_OFF + VST * TILE_BYTES;
-  static constexpr int NUM_BARS = 1 + 2 * KST + 2 * VST + 3 * NQ + 1;
+  // One ring of K and V tiles in load order K_0 V_0 K_1 V_1 ...: as many
+  // slots as fit (5 at D = 128), so loads run about 1.5 key tiles ahead.
+  static constexpr int RING_OFF = Q_OFF + NQ * TILE_BYTES;
+  static constexpr int SLOTS_FIT = (227 * 1024 - 1024 - RING_OFF - 512) / TILE_BYTES;
+  static constexpr int SLOTS = SLOTS_FIT < 8 ? SLOTS_FIT : 8;
+  static constexpr int BAR_OFF = RING_OFF + SLOTS * TILE_BYTES;
+  static constexpr int NUM_BARS = 1 + 2 * SLOTS + 4 * NQ + 1;
+  static_assert(SLOTS >= 3, "K/V ring");
   static constexpr int MISC_OFF = BAR_OFF + NUM_BARS * 8;
   static constexpr int SMEM_ALLOC = MISC_OFF + 16 + 1024;  // + slack to align the base to 1 KB
   static constexpr int SOFT_WARPS = 4 * NQ;
@@ -134,13 +141,11 @@ __global__ void __launch_bounds__(TcCfg<D, NQ>::THREADS, 1)
       (reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~static_cast<uintptr_t>(1023));
   uint64_t* bars = reinterpret_cast<uint64_t*>(smem + C::BAR_OFF);
   uint64_t* q_full = bars;
-  uint64_t* k_full = q_full + 1;
-  uint64_t* k_empty = k_full + C::KST;
-  uint64_t* v_full = k_empty + C::KST;
-  uint64_t* v_empty = v_full + C::VST;
-  uint64_t* s_full = v_empty + C::VST;  // MMA -> softmax: S_i ready
-  uint64_t* p_full = s_full + NQ;       // softmax -> MMA: P_i written (and O_i rescaled)
-  uint64_t* o_full = p_full + NQ;       // MMA -> softmax: O_i += P_i V done
+  uint64_t* full = q_full + 1;           // ring slot loaded (TMA transaction count)
+  uint64_t* empty = full + C::SLOTS;     // ring slot released by the MMAs that read it
+  uint64_t* s_full = empty + C::SLOTS;   // MMA -> softmax: S_i ready
+  uint64_t* p_full = s_full + NQ;       // softmax -> MMA: half h of P_i written (2 i + h)
+  uint64_t* o_full = p_full + 2 * NQ;   // MMA -> softmax: O_i += P_i V done
   uint64_t* drain = o_full + NQ;
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(smem + C::MISC_OFF);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(smem + C::MISC_OFF + 4);
@@ -153,17 +158,14 @@ __global__ void __launch_bounds__(TcCfg<D, NQ>::THREADS, 1)
 
   if (threadIdx.x == 0) {
     mbar_init(q_full, 1);
-    for (int s = 0; s < C::KST; ++s) {
-      mbar_init(k_full + s, 1);
-      mbar_init(k_empty + s, 1);
-    }
-    for (int s = 0; s < C::VST; ++s) {
-      mbar_init(v_full + s, 1);
-      mbar_init(v_empty + s, 1);
+    for (int s = 0; s < C::SLOTS; ++s) {
+      mbar_init(full + s, 1);
+      mbar_init(empty + s, 1);
     }
     for (int i = 0; i < NQ; ++i) {
       mbar_init(s_full + i, 1);
-      mbar_init(p_full + i, 128);
+      mbar_init(p_full + 2 * i, 4);  // one arrival per softmax warp
+      mbar_init(p_full + 2 * i + 1, 4);
       mbar_init(o_full + i, 1);
     }
     mbar_init(drain, 1);
@@ -198,39 +200,28 @@ __global__ void __launch_bounds__(TcCfg<D, NQ>::THREADS, 1)
         for (int h = 0; h < C::NHALF; ++h)
           tma_load_3d(smem + C::Q_OFF + i * C::TILE_BYTES + h * C::BLK_BYTES, &p.tq, q_full,
                       h * 64, (qt0 + i) * kBM, bh);
-      int k_issued = 0, v_issued = 0;
-      for (int j = 0; j < nkv_max; ++j) {
-        const int ks = j % C::KST;
-        if (!mbar_wait(k_empty + ks, ((j / C::KST) & 1) ^ 1, abort_flag, p.status, kSiteLoadK,
-                       p.timeout_ns))
+      // Item 2 j is K_j and item 2 j + 1 is V_j; item `it` goes to slot
+      // it % SLOTS on its (it / SLOTS)-th use of that slot.
+      int issued = 0;
+      for (int it = 0; it < 2 * nkv_max; ++it) {
+        const int slot = it % C::SLOTS;
+        if (!mbar_wait(empty + slot, ((it / C::SLOTS) & 1) ^ 1, abort_flag, p.status,
+                       (it & 1) ? kSiteLoadV : kSiteLoadK, p.timeout_ns))
           break;
-        mbar_arrive_expect_tx(k_full + ks, C::TILE_BYTES);
+        mbar_arrive_expect_tx(full + slot, C::TILE_BYTES);
+        const CUtensorMap* map = (it & 1) ? &p.tv : &p.tk;
         for (int h = 0; h < C::NHALF; ++h)
-          tma_load_3d(smem + C::K_OFF + ks * C::TILE_BYTES + h * C::BLK_BYTES, &p.tk,
-                      k_full + ks, h * 64, j * kBN, bh);
-        ++k_issued;
-        const int vs = j % C::VST;
-        if (!mbar_wait(v_empty + vs, ((j / C::VST) & 1) ^ 1, abort_flag, p.status, kSiteLoadV,
-                       p.timeout_ns))
-          break;
-        mbar_arrive_expect_tx(v_full + vs, C::TILE_BYTES);
-        for (int h = 0; h < C::NHALF; ++h)
-          tma_load_3d(smem + C::V_OFF + vs * C::TILE_BYTES + h * C::BLK_BYTES, &p.tv,
-                      v_full + vs, h * 64, j * kBN, bh);
-        ++v_issued;
+          tma_load_3d(smem + C::RING_OFF + slot * C::TILE_BYTES + h * C::BLK_BYTES, map,
+                      full + slot, h * 64, (it >> 1) * kBN, bh);
+        ++issued;
       }
       // Never leave with a copy in flight: wait (bounded, regardless of the
       // abort flag) for the last phase issued on every full barrier.
       mbar_wait(q_full, 0, nullptr, p.status, kSiteDrainLoads, p.timeout_ns);
-      for (int s = 0; s < C::KST; ++s) {
-        const int cnt = k_issued > s ? (k_issued - 1 - s) / C::KST + 1 : 0;
+      for (int sl = 0; sl < C::SLOTS; ++sl) {
+        const int cnt = issued > sl ? (issued - 1 - sl) / C::SLOTS + 1 : 0;
         if (cnt > 0)
-          mbar_wait(k_full + s, (cnt - 1) & 1, nullptr, p.status, kSiteDrainLoads, p.timeout_ns);
-      }
-      for (int s = 0; s < C::VST; ++s) {
-        const int cnt = v_issued > s ? (v_issued - 1 - s) / C::VST + 1 : 0;
-        if (cnt > 0)
-          mbar_wait(v_full + s, (cnt - 1) & 1, nullptr, p.status, kSiteDrainLoads, p.timeout_ns);
+          mbar_wait(full + sl, (cnt - 1) & 1, nullptr, p.status, kSiteDrainLoads, p.timeout_ns);
       }
     }
   } else if (warp == C::MMA_WARP) {
@@ -239,16 +230,19 @@ __global__ void __launch_bounds__(TcCfg<D, NQ>::THREADS, 1)
       constexpr uint32_t kIdescS = idesc_f16_f32(kBM, kBN, false, false);
       constexpr uint32_t kIdescO = idesc_f16_f32(kBM, D, false, true);
       const uint32_t q_base = smem_u32(smem + C::Q_OFF);
-      const uint32_t k_base = smem_u32(smem + C::K_OFF);
-      const uint32_t v_base = smem_u32(smem + C::V_OFF);
+      const uint32_t ring_base = smem_u32(smem + C::RING_OFF);
+      auto item_addr = [&](int it) { return ring_base + (it % C::SLOTS) * C::TILE_BYTES; };
+      auto wait_item = [&](int it) {
+        return mbar_wait(full + it % C::SLOTS, (it / C::SLOTS) & 1, abort_flag, p.status,
+                         (it & 1) ? kSiteMmaV : kSiteMmaK, p.timeout_ns);
+      };
       int nkv[NQ];
 #pragma unroll
       for (int i = 0; i < NQ; ++i) nkv[i] = kv_tiles_of(p, qt0 + i);
 
       // S_i = Q_i K^T: K = D in steps of 16 (32 bytes inside a 128-byte swizzle row).
-      auto issue_s = [&](int i, int ks) {
+      auto issue_s = [&](int i, uint32_t b0) {
         const uint32_t a0 = q_base + i * C::TILE_BYTES;
-        const uint32_t b0 = k_base + ks * C::TILE_BYTES;
 #pragma unroll
         for (int kk = 0; kk < D / 16; ++kk) {
           const uint32_t off = (kk >> 2) * C::BLK_BYTES + (kk & 3) * 32;
@@ -258,10 +252,10 @@ __global__ void __launch_bounds__(TcCfg<D, NQ>::THREADS, 1)
       };
       // O_i (+)= P_i V: K = 128 keys in steps of 16 rows (2 KB of V); V is
       // MN-major, the 64-column blocks 16 KB apart (LBO), 8-row groups 1 KB (SBO).
-      auto issue_pv = [&](int i, int vs, bool accumulate) {
-        const uint32_t b0 = v_base + vs * C::TILE_BYTES;
+      // Half h covers keys [64 h, 64 h + 64): P columns [32 h, 32 h + 32).
+      auto issue_pv = [&](int i, uint32_t b0, int h, bool accumulate) {
 #pragma unroll
-        for (int kk = 0; kk < kBN / 16; ++kk) {
+        for (int kk = 4 * h; kk < 4 * h + 4; ++kk) {
           mma_f16_ts(tmem + C::O_COL + i * D, tmem + i * kBN + kk * 8,
                      sdesc_sw128(b0 + kk * 2048, C::BLK_BYTES, 1024), kIdescO,
                      (accumulate || kk > 0) ? 1u : 0u);
@@ -269,51 +263,53 @@ __global__ void __launch_bounds__(TcCfg<D, NQ>::THREADS, 1)
       };
 
       bool ok = mbar_wait(q_full, 0, abort_flag, p.status, kSiteMmaQ, p.timeout_ns) &&
-                mbar_wait(k_full, 0, abort_flag, p.status, kSiteMmaK, p.timeout_ns);
+                wait_item(0);
       if (ok) {
         tc_fence_after();
 #pragma unroll
         for (int i = 0; i < NQ; ++i) {
           if (nkv[i] > 0) {
-            issue_s(i, 0);
+            issue_s(i, item_addr(0));
             tc_commit(s_full + i);
           }
         }
-        tc_commit(k_empty);
+        tc_commit(empty + 0);
       }
       for (int j = 0; ok && j < nkv_max; ++j) {
-        const int vs = j % C::VST;
-        ok = mbar_wait(v_full + vs, (j / C::VST) & 1, abort_flag, p.status, kSiteMmaV,
-                       p.timeout_ns);
+        const int v_it = 2 * j + 1, k_it = 2 * j + 2;  // V_j, K_{j+1}
+        ok = wait_item(v_it);
         if (!ok) break;
         tc_fence_after();
         const bool next = j + 1 < nkv_max;
-        const int ks = (j + 1) % C::KST;
         bool k_ready = false;
 #pragma unroll
         for (int i = 0; i < NQ; ++i) {
           if (j < nkv[i]) {
-            ok = mbar_wait(p_full + i, j & 1, abort_flag, p.status, kSiteMmaP, p.timeout_ns);
+            ok = mbar_wait(p_full + 2 * i, j & 1, abort_flag, p.status, kSiteMmaP, p.timeout_ns);
             if (!ok) break;
             tc_fence_after();
-            issue_pv(i, vs, j > 0);
+            issue_pv(i, item_addr(v_it), 0, j > 0);
+            ok = mbar_wait(p_full + 2 * i + 1, j & 1, abort_flag, p.status, kSiteMmaP,
+                           p.timeout_ns);
+            if (!ok) break;
+            tc_fence_after();
+            issue_pv(i, item_addr(v_it), 1, true);
             tc_commit(o_full + i);
           }
           if (next && j + 1 < nkv[i]) {
             if (!k_ready) {
-              ok = mbar_wait(k_full + ks, ((j + 1) / C::KST) & 1, abort_flag, p.status, kSiteMmaK,
-                             p.timeout_ns);
+              ok = wait_item(k_it);
               if (!ok) break;
               tc_fence_after();
               k_ready = true;
             }
-            issue_s(i, ks);
+            issue_s(i, item_addr(k_it));
             tc_commit(s_full + i);
           }
         }
         if (!ok) break;
-        tc_commit(v_empty + vs);
-        if (next && k_ready) tc_commit(k_empty + ks);
+        tc_commit(empty + v_it % C::SLOTS);
+        if (next && k_ready) tc_commit(empty + k_it % C::SLOTS);
       }
       // Every MMA issued completes before tensor memory is released.
       tc_commit(drain);
@@ -349,45 +345,86 @@ __global__ void __launch_bounds__(TcCfg<D, NQ>::THREADS, 1)
         if (!ok) break;
         tc_fence_after();
         // One register array for the row: fp32 scores in, packed fp16 P out
-        // (P pair c overwrites slot c, whose score was consumed at pair c / 2).
+        // (P pair c overwrites slot c, whose scores were consumed at pair c).
         // With a positive scale the max is taken on the raw scores and the
         // scale is folded into the exponent's FMA; otherwise the row is
         // scaled first.
         uint32_t sr[kBN];
-        tmem_ld128_wait(t_s, sr);
         float cs = p.scale_log2;
-        if (cs <= 0.f) {
-#pragma unroll
-          for (int c = 0; c < kBN; c += 2) {
-            float a, b;
-            f2_unpack(f2_mul(f2_pack(__uint_as_float(sr[c]), __uint_as_float(sr[c + 1])),
-                             f2_pack(cs, cs)), a, b);
-            sr[c] = __float_as_uint(a);
-            sr[c + 1] = __float_as_uint(b);
-          }
-          cs = 1.f;
-        }
         const int k0 = j * kBN;
-        if ((p.causal && j == qt) || k0 + kBN > p.n) {
-          const int lim = p.causal ? min(q_row + 1, p.n) : p.n;  // keys [0, lim) are visible
+        auto load_row = [&]() {
+          tmem_ld128_wait(t_s, sr);
+          cs = p.scale_log2;
+          if (cs <= 0.f) {
 #pragma unroll
-          for (int c = 0; c < kBN; ++c)
-            if (k0 + c >= lim) sr[c] = __float_as_uint(-INFINITY);
-        }
-        float mt0 = fmax3(__uint_as_float(sr[0]), __uint_as_float(sr[1]), __uint_as_float(sr[2]));
-        float mt1 = fmax3(__uint_as_float(sr[3]), __uint_as_float(sr[4]), __uint_as_float(sr[5]));
-        float mt2 = fmax3(__uint_as_float(sr[6]), __uint_as_float(sr[7]), __uint_as_float(sr[8]));
-        float mt3 = fmax3(__uint_as_float(sr[9]), __uint_as_float(sr[10]), __uint_as_float(sr[11]));
+            for (int c = 0; c < kBN; c += 2) {
+              float a, b;
+              f2_unpack(f2_mul(f2_pack(__uint_as_float(sr[c]), __uint_as_float(sr[c + 1])),
+                               f2_pack(cs, cs)), a, b);
+              sr[c] = __float_as_uint(a);
+              sr[c + 1] = __float_as_uint(b);
+            }
+            cs = 1.f;
+          }
+          if ((p.causal && j == qt) || k0 + kBN > p.n) {
+            const int lim = p.causal ? min(q_row + 1, p.n) : p.n;  // keys [0, lim) are visible
 #pragma unroll
-        for (int c = 12; c + 8 <= kBN; c += 8) {
-          mt0 = fmax3(mt0, __uint_as_float(sr[c]), __uint_as_float(sr[c + 1]));
-          mt1 = fmax3(mt1, __uint_as_float(sr[c + 2]), __uint_as_float(sr[c + 3]));
-          mt2 = fmax3(mt2, __uint_as_float(sr[c + 4]), __uint_as_float(sr[c + 5]));
-          mt3 = fmax3(mt3, __uint_as_float(sr[c + 6]), __uint_as_float(sr[c + 7]));
-        }
-        mt0 = fmax3(mt0, __uint_as_float(sr[kBN - 4]), __uint_as_float(sr[kBN - 3]));
-        mt1 = fmax3(mt1, __uint_as_float(sr[kBN - 2]), __uint_as_float(sr[kBN - 1]));
-        const float m_new = fmaxf(m, fmax3(mt0, mt1, fmaxf(mt2, mt3)) * cs);
+            for (int c = 0; c < kBN; ++c)
+              if (k0 + c >= lim) sr[c] = __float_as_uint(-INFINITY);
+          }
+        };
+        // P = 2^(cs * s - m) in two halves of 64 keys; each half is stored and
+        // handed to the MMA warp at once, so P V on the first half overlaps the
+        // exponentials of the second. In each half the last kPolyCols / 2
+        // columns go to the FMA pipe (f2_exp2_poly), the rest to the MUFU.
+        uint64_t cs2, nm2, rs0, rs1;
+        auto start_exps = [&]() {
+          const float m_use = (m == -INFINITY) ? 0.f : m;
+          cs2 = f2_pack(cs, cs);
+          nm2 = f2_pack(-m_use, -m_use);
+          rs0 = f2_pack(0.f, 0.f);
+          rs1 = rs0;
+        };
+        auto exp_pair = [&](int c) {  // pair c: scores 2c, 2c+1 -> packed fp16 in sr[c]
+          const uint64_t x =
+              f2_fma(f2_pack(__uint_as_float(sr[2 * c]), __uint_as_float(sr[2 * c + 1])), cs2, nm2);
+          if constexpr (kExpHalf2) {
+            // One MUFU op for the pair, in fp16 (the precision P is kept in);
+            // the row sum adds the same rounded values in fp32.
+            float a, b;
+            f2_unpack(x, a, b);
+            const uint32_t ph = fast_exp2_h2(pack_half2(a, b));
+            const float2 pf = __half22float2(*reinterpret_cast<const __half2*>(&ph));
+            if (c & 1) rs1 = f2_add(rs1, f2_pack(pf.x, pf.y)); else rs0 = f2_add(rs0, f2_pack(pf.x, pf.y));
+            sr[c] = ph;
+          } else {
+            uint64_t pr;
+            if ((2 * c) % (kBN / 2) < kBN / 2 - kPolyCols / 2) {
+              float a, b;
+              f2_unpack(x, a, b);
+              pr = f2_pack(fast_exp2(a), fast_exp2(b));
+            } else {
+              pr = f2_exp2_poly(x);
+            }
+            if (c & 1) rs1 = f2_add(rs1, pr); else rs0 = f2_add(rs0, pr);
+            float a, b;
+            f2_unpack(pr, a, b);
+            sr[c] = pack_half2(a, b);
+          }
+        };
+        float mt[8];
+        auto row_max = [&]() {
+          return fmax3(fmax3(mt[0], mt[1], mt[2]), fmax3(mt[3], mt[4], mt[5]), fmaxf(mt[6], mt[7])) * cs;
+        };
+        load_row();
+#pragma unroll
+        for (int a = 0; a < 8; ++a)
+          mt[a] = fmax3(__uint_as_float(sr[3 * a]), __uint_as_float(sr[3 * a + 1]),
+                        __uint_as_float(sr[3 * a + 2]));
+#pragma unroll
+        for (int c = 24; c < kBN; c += 2)
+          mt[(c / 2) & 7] = fmax3(mt[(c / 2) & 7], __uint_as_float(sr[c]), __uint_as_float(sr[c + 1]));
+        const float m_new = fmaxf(m, row_max());
         if (j == 0) {
           m = m_new;
         } else if (__any_sync(0xffffffffu, m_new > m + kRescaleThreshold)) {
@@ -416,40 +453,27 @@ __global__ void __launch_bounds__(TcCfg<D, NQ>::THREADS, 1)
           l *= alpha;
           m = m_new;
         }
-        // P = 2^(cs * s - m): packed FMAs; the first columns on the MUFU, the
-        // last kPolyCols on the FMA pipe (f2_exp2_poly), to share the load.
-        const float m_use = (m == -INFINITY) ? 0.f : m;
-        const uint64_t cs2 = f2_pack(cs, cs);
-        const uint64_t nm2 = f2_pack(-m_use, -m_use);
-        uint64_t rs0 = f2_pack(0.f, 0.f), rs1 = rs0;
+        start_exps();
 #pragma unroll
-        for (int c = 0; c < kBN / 2; ++c) {
-          const uint64_t x =
-              f2_fma(f2_pack(__uint_as_float(sr[2 * c]), __uint_as_float(sr[2 * c + 1])), cs2, nm2);
-          uint64_t pr;
-          if (2 * c < kBN - kPolyCols) {
-            float a, b;
-            f2_unpack(x, a, b);
-            pr = f2_pack(fast_exp2(a), fast_exp2(b));
-          } else {
-            pr = f2_exp2_poly(x);
-          }
-          if (c & 1) rs1 = f2_add(rs1, pr); else rs0 = f2_add(rs0, pr);
-          float a, b;
-          f2_unpack(pr, a, b);
-          sr[c] = pack_half2(a, b);
-        }
+        for (int c = 0; c < kBN / 4; ++c) exp_pair(c);
+        tmem_st32<0>(t_s, sr);
+        tmem_st_wait();
+        tc_fence_before();
+        __syncwarp();
+        if (lane == 0) mbar_arrive(p_full + 2 * wg);
+#pragma unroll
+        for (int c = kBN / 4; c < kBN / 2; ++c) exp_pair(c);
+        tmem_st32<32>(t_s + 32, sr);
+        tmem_st_wait();
+        tc_fence_before();
+        __syncwarp();
+        if (lane == 0) mbar_arrive(p_full + 2 * wg + 1);
         {
           float a, b, c2, d2;
           f2_unpack(rs0, a, b);
           f2_unpack(rs1, c2, d2);
           l += (a + b) + (c2 + d2);
         }
-        tmem_st32<0>(t_s, sr);
-        tmem_st32<32>(t_s + 32, sr);
-        tmem_st_wait();
-        tc_fence_before();
-        mbar_arrive(p_full + wg);
       }
       if (ok) {
         ok = mbar_wait(o_full + wg, (n_i - 1) & 1, abort_flag, p.status, kSiteEpilogue,
