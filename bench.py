@@ -116,6 +116,21 @@ class Dist:
         self.dist.all_reduce(t, op=self.dist.ReduceOp.MAX)
         return float(t.item())
 
+    def sum(self, x: float) -> float:
+        if self.world == 1:
+            return x
+        t = torch.tensor([x], dtype=torch.float64, device=self.device)
+        self.dist.all_reduce(t, op=self.dist.ReduceOp.SUM)
+        return float(t.item())
+
+    def gather(self, x: float) -> list:
+        if self.world == 1:
+            return [x]
+        t = torch.tensor([x], dtype=torch.float64, device=self.device)
+        out = torch.empty(self.world, dtype=torch.float64, device=self.device)
+        self.dist.all_gather_into_tensor(out, t)
+        return [round(float(v), 4) for v in out.tolist()]
+
     def close(self):
         if self.world > 1:
             self.dist.destroy_process_group()
@@ -175,8 +190,9 @@ class ClockSampler:
                 "reasons": sorted(reasons), "samples": len(sm)}
 
 
-def timed(fn, steps, warmup, d: Dist, spin_s=0.0):
+def timed(fn, steps, warmup, d: Dist, spin_s=0.0, per_rank=None):
     """ms for exactly `steps` calls of fn (max over ranks), after `warmup` calls.
+    If `per_rank` is a list, every rank's own ms is appended to it.
 
     spin_s: keep the GPU busy with untimed calls for about this long first, so
     the clock samples taken meanwhile reflect the loaded state."""
@@ -198,7 +214,10 @@ def timed(fn, steps, warmup, d: Dist, spin_s=0.0):
     end.record(stream)
     torch.cuda.synchronize(d.device)
     d.barrier()
-    return d.max(start.elapsed_time(end))
+    mine = start.elapsed_time(end)
+    if per_rank is not None:
+        per_rank.extend(d.gather(mine))
+    return d.max(mine)
 
 
 def roofline(bound, work_per_launch, ms_per_launch, peaks, peak_src, traffic=None):
@@ -248,8 +267,9 @@ def bench_prefill_cfg2(args, d: Dist, peaks, peak_src, traffic):
     gen = torch.Generator(device=d.device).manual_seed(1000 + d.rank)
     q, k, v = (randn_half(shape, gen, d.device) for _ in range(3))
     fn = lambda: ak.flash_attention(q, k, v, causal=True)  # noqa: E731
+    ranks_ms = []
     with ClockSampler(d.local) as clk:
-        ms = timed(fn, args.steps, args.warmup, d, spin_s=args.spin)
+        ms = timed(fn, args.steps, args.warmup, d, spin_s=args.spin, per_rank=ranks_ms)
     flops = prefill_flops(**c)
     res = {
         "ms_per_step": ms / args.steps,
@@ -258,6 +278,7 @@ def bench_prefill_cfg2(args, d: Dist, peaks, peak_src, traffic):
                              traffic.get("flash_tc_kernel_cfg2")),
         "clocks": clk.summary(),
         "gpu_launches": args.steps,  # one flash_tc_kernel launch per step
+        "per_rank_ms_per_step": [round(x / args.steps, 4) for x in ranks_ms],
     }
     # End to end through the public API: pinned host q, k, v -> device, attention,
     # output -> pinned host, every step.
@@ -294,9 +315,11 @@ def bench_decode_cfg4(args, d: Dist, peaks, peak_src, traffic):
     max_ctx = max(ctx)
     fn = lambda: ak.paged_decode(q, kc, vc, tables, lens, max_ctx,  # noqa: E731
                                  partition_size=c["partition"])
+    ranks_ms = []
     with ClockSampler(d.local) as clk:
-        ms = timed(fn, args.steps, args.warmup, d, spin_s=args.spin)
+        ms = timed(fn, args.steps, args.warmup, d, spin_s=args.spin, per_rank=ranks_ms)
     nbytes = kv_bytes(ctx, c["kv_heads"], c["head_dim"])
+    total_bytes = d.sum(nbytes)  # each rank decodes its own seeded batch
     res = {
         "config": {"workload": "paged decode, BASELINE config 4", "batch": c["batch"],
                    "heads": c["heads"], "kv_heads": c["kv_heads"], "head_dim": c["head_dim"],
@@ -305,7 +328,8 @@ def bench_decode_cfg4(args, d: Dist, peaks, peak_src, traffic):
                    "l2": "inputs larger than L2 (KV %.2f GB)" % (nbytes / 1e9)},
         "metric": "paged-decode KV GB/s", "unit": "GB/s",
         "ms_per_step": ms / args.steps,
-        "value": nbytes * d.world / (ms / args.steps * 1e-3) / 1e9,
+        "value": total_bytes / (ms / args.steps * 1e-3) / 1e9,
+        "per_rank_ms_per_step": [round(x / args.steps, 4) for x in ranks_ms],
         # The timed op is memset + decode kernel + merge kernel: the kernel's own
         # time is lower, so this fraction is a lower bound.
         "roofline": roofline("hbm", nbytes, ms / args.steps, peaks, peak_src,
@@ -325,7 +349,7 @@ def bench_decode_cfg4(args, d: Dist, peaks, peak_src, traffic):
                  non_blocking=True)
 
     ms_e2e = timed(e2e, args.steps, args.warmup, d)
-    res["e2e"] = {"value": round(nbytes * d.world / (ms_e2e / args.steps * 1e-3) / 1e9, 1),
+    res["e2e"] = {"value": round(total_bytes / (ms_e2e / args.steps * 1e-3) / 1e9, 1),
                   "unit": "GB/s", "ms_per_step": round(ms_e2e / args.steps, 4),
                   "h2d_bytes_per_step": hq.numel() * 2 + htab.numel() * 4 + hlen.numel() * 4,
                   "d2h_bytes_per_step": ho.numel() * 2,
@@ -492,6 +516,44 @@ def profile_case(kind, d: Dist):
     ak.check_device_status(d.device)
 
 
+def split_ablation(args, d: Dist):
+    """Decode GB/s versus partition size (the reference's split ablation,
+    bench/bench.py:274-280, on B200 shapes): config 4, config 5 on one GPU, and
+    one rank's share of config 5 at 8 GPUs (partials + local merge, no exchange)."""
+    import attnkernels as ak
+    from attnkernels import parallel
+
+    rows = []
+    cases = []
+    c = CFG4
+    g = torch.Generator().manual_seed(4000)
+    ctx4 = torch.randint(c["ctx_lo"], c["ctx_hi"] + 1, (c["batch"],), generator=g).tolist()
+    cases.append(("config4", ctx4, False))
+    c5 = CFG5
+    cases.append(("config5_1gpu", [c5["ctx"]] * c5["batch"], False))
+    t0, t1 = parallel.context_range(c5["ctx"], c5["block_size"], 8, 0)
+    cases.append(("config5_rank_of_8", [t1 - t0] * c5["batch"], True))
+    for name, ctx, partial in cases:
+        kc, vc, tables, lens = synthetic_paged_cache(ctx, 32, 128, 16, 7, d.device)
+        q = randn_half((len(ctx), 32, 128), torch.Generator(device=d.device).manual_seed(3), d.device)
+        nbytes = kv_bytes(ctx, 32, 128)
+        for part in [256, 512, 1024, 2048, 4096, None]:
+            pp = part if part is not None else ak.decode_partition(len(ctx), 32, max(ctx))
+            if partial:
+                fn = lambda: ak.paged_decode_partials(q, kc, vc, tables, lens, max(ctx),  # noqa: E731
+                                                      partition_size=pp)
+            else:
+                fn = lambda: ak.paged_decode(q, kc, vc, tables, lens, max(ctx),  # noqa: E731
+                                             partition_size=pp)
+            ms = timed(fn, args.steps, args.warmup, d) / args.steps
+            rows.append({"case": name, "partition": pp, "auto": part is None,
+                         "splits": -(-max(ctx) // pp), "ms": round(ms, 4),
+                         "gbps": round(nbytes / (ms * 1e-3) / 1e9, 1)})
+        del kc, vc
+        torch.cuda.empty_cache()
+    return rows
+
+
 def main():
     ap = argparse.ArgumentParser(description="attention hot paths on B200")
     ap.add_argument("--gpus", type=int, default=1)
@@ -503,6 +565,8 @@ def main():
     ap.add_argument("--only-prefill", action="store_true", help="headline kernel only")
     ap.add_argument("--spin", type=float, default=1.0,
                     help="seconds of untimed load before a timed region (clock sampling)")
+    ap.add_argument("--ablation", action="store_true",
+                    help="print the decode split-size ablation (one JSON list) and exit")
     ap.add_argument("--profile", choices=["prefill", "decode"],
                     help="run one small case of a kernel (3 + 2 launches) for ncu, no timing")
     args = ap.parse_args()
@@ -521,6 +585,11 @@ def main():
     ak.load_extension()  # fails loudly without the native library
     if args.profile:
         profile_case(args.profile, d)
+        return
+    if args.ablation:
+        rows = split_ablation(args, d)
+        if d.rank == 0:
+            print(json.dumps({"split_ablation": rows}), flush=True)
         return
     peaks, peak_src = load_peaks()
     traffic = load_traffic()
@@ -546,6 +615,7 @@ def main():
         "roofline": pre["roofline"],
         "e2e": pre["e2e"],
         "gpu_launches": pre["gpu_launches"],
+        "per_rank_ms_per_step": pre["per_rank_ms_per_step"],
         "clocks": pre["clocks"],
     }
     if not args.only_prefill:

@@ -43,9 +43,12 @@ CHUNK = 256
 WMMA_BLOCK_N = {64: 64, 128: 64}
 
 # Decode work units (sequence, kv head, split) to aim for per resident warp of
-# the decode kernel, and its resident warps per SM.
-_UNITS_PER_WARP = 16
+# the decode kernel, its resident warps per SM, and the most splits of one
+# sequence (each split adds a part to that row's merge). Chosen from the split
+# ablation on B200 (bench.py --ablation).
+_UNITS_PER_WARP = 32
 _DECODE_WARPS_PER_SM = 8
+_MAX_SPLITS = 32
 
 
 @functools.lru_cache(maxsize=None)
@@ -102,7 +105,8 @@ def decode_partition(batch, num_kv_heads, max_context_len, device=None, sm_count
     least one chunk per split, more splits when batch * kv heads is small), with
     the B200 target: about _UNITS_PER_WARP (sequence, kv head, split) units per
     resident decode warp (8 per SM), so the persistent kernel balances ragged
-    batches. `sm_count` overrides the device query.
+    batches, and at most _MAX_SPLITS splits per sequence, which bounds the merge.
+    `sm_count` overrides the device query.
     """
     if sm_count is None:
         dev = torch.cuda.current_device() if device is None else device
@@ -110,7 +114,7 @@ def decode_partition(batch, num_kv_heads, max_context_len, device=None, sm_count
     units = max(1, batch * num_kv_heads)
     want = -(-_UNITS_PER_WARP * _DECODE_WARPS_PER_SM * sm_count // units)
     max_chunks = max(1, -(-max_context_len // CHUNK))
-    splits = max(1, min(want, max_chunks))
+    splits = max(1, min(want, max_chunks, _MAX_SPLITS))
     return -(-max_chunks // splits) * CHUNK
 
 

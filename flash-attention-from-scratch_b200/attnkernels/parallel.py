@@ -71,16 +71,41 @@ class ContextParallelDecode:
     partials_fn(q, kc, vc, bt, lens, max_len, scale, partition, out=(o, m, l))
     fills o [B, H, D], m and l [B, H] (fp32); merge_fn(o_parts, m_parts,
     l_parts) merges [P, B, H, D] / [P, B, H] views. Defaults: the CUDA kernels.
+
+    chunks > 1 (CUDA tensors only) splits the batch: the all-gather of one
+    chunk's partials runs on a side stream while the next chunk is decoded, so
+    only the last chunk's exchange and the merges are exposed.
     """
 
-    def __init__(self, group=None, partials_fn=None, merge_fn=None):
+    def __init__(self, group=None, partials_fn=None, merge_fn=None, chunks=1):
         self.group = group
+        self.custom_merge = merge_fn is not None
         if partials_fn is None or merge_fn is None:
             from . import merge_partials, paged_decode_partials
             partials_fn = partials_fn or paged_decode_partials
             merge_fn = merge_fn or merge_partials
         self.partials_fn = partials_fn
         self.merge_fn = merge_fn
+        self.chunks = max(1, int(chunks))
+        self._comm = {}
+
+    @staticmethod
+    def _views(buf, rows_b, heads, d):
+        rows = rows_b * heads
+        return (buf[..., : rows * d].unflatten(-1, (rows_b, heads, d)),
+                buf[..., rows * d: rows * (d + 1)].unflatten(-1, (rows_b, heads)),
+                buf[..., rows * (d + 1): rows * (d + 2)].unflatten(-1, (rows_b, heads)))
+
+    def _exchange(self, q, k_cache, v_cache, block_tables, context_lens, max_context_len,
+                  scale, partition_size, world):
+        B, H, D = q.shape
+        # One fp32 buffer per rank: o [rows, D], m [rows], l [rows], padded to
+        # 16 bytes so every part's o rows stay 16-byte aligned after the gather.
+        stride = -(-(B * H * (D + 2)) // 4) * 4
+        buf = torch.empty(stride, dtype=torch.float32, device=q.device)
+        self.partials_fn(q, k_cache, v_cache, block_tables, context_lens, max_context_len,
+                         scale, partition_size, out=self._views(buf, B, H, D))
+        return buf
 
     def __call__(self, q, k_cache, v_cache, block_tables, context_lens, max_context_len,
                  scale=None, partition_size=None):
@@ -88,18 +113,30 @@ class ContextParallelDecode:
         if q.dim() == 4:
             q = q.reshape(q.shape[0], q.shape[1], q.shape[3])
         B, H, D = q.shape
-        rows = B * H
-        # One fp32 buffer per rank: o [rows, D], m [rows], l [rows], padded to
-        # 16 bytes so every part's o rows stay 16-byte aligned after the gather.
-        stride = -(-(rows * (D + 2)) // 4) * 4
-        buf = torch.empty(stride, dtype=torch.float32, device=q.device)
-        o = buf[: rows * D].view(B, H, D)
-        m = buf[rows * D: rows * (D + 1)].view(B, H)
-        l = buf[rows * (D + 1): rows * (D + 2)].view(B, H)
-        self.partials_fn(q, k_cache, v_cache, block_tables, context_lens, max_context_len,
-                         scale, partition_size, out=(o, m, l))
-        gathered = _gather_flat(buf, world, self.group)
-        o_parts = gathered[:, : rows * D].view(world, B, H, D)
-        m_parts = gathered[:, rows * D: rows * (D + 1)].view(world, B, H)
-        l_parts = gathered[:, rows * (D + 1): rows * (D + 2)].view(world, B, H)
-        return self.merge_fn(o_parts, m_parts, l_parts)
+        nchunks = min(self.chunks, B) if q.is_cuda and not self.custom_merge else 1
+        if nchunks == 1:
+            buf = self._exchange(q, k_cache, v_cache, block_tables, context_lens,
+                                 max_context_len, scale, partition_size, world)
+            gathered = _gather_flat(buf, world, self.group)
+            return self.merge_fn(*self._views(gathered, B, H, D))
+        compute = torch.cuda.current_stream(q.device)
+        comm = self._comm.get(q.device)
+        if comm is None:
+            comm = self._comm[q.device] = torch.cuda.Stream(q.device)
+        out = torch.empty(B, H, D, dtype=torch.float16, device=q.device)
+        pending = []
+        for c in range(nchunks):
+            b0, b1 = shard_range(B, nchunks, c)
+            buf = self._exchange(q[b0:b1], k_cache, v_cache, block_tables[b0:b1],
+                                 context_lens[b0:b1], max_context_len, scale, partition_size,
+                                 world)
+            comm.wait_stream(compute)
+            with torch.cuda.stream(comm):
+                gathered = _gather_flat(buf, world, self.group)
+            buf.record_stream(comm)
+            gathered.record_stream(compute)
+            pending.append((b0, b1, gathered))
+        compute.wait_stream(comm)
+        for b0, b1, gathered in pending:
+            self.merge_fn(*self._views(gathered, b1 - b0, H, D), out=out[b0:b1])
+        return out

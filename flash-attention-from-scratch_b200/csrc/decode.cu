@@ -451,23 +451,46 @@ __global__ void __launch_bounds__(256) merge_partials_kernel(const MergeParams p
   for (int j = 0; j < DV; ++j) num[j] = 0.f;
   float den = 0.f;
   if (mx != -INFINITY) {
+    // Parts in groups of 32: lane s holds the weight of part s0 + s; the
+    // weights are broadcast by shuffles while eight part rows are loaded at
+    // once, so the loads of a row's parts overlap instead of forming a chain.
     const float* orow = p.o + row * p.o_row_stride + lane * DV;
-    for (int s = 0; s < ns; ++s) {
-      const float w = lrow[s * p.ml_part_stride] * fast_exp2(mrow[s * p.ml_part_stride] - mx);
-      den += w;
-      const float* src = orow + s * p.o_part_stride;
-      if constexpr (DV == 4) {
-        const float4 v = *reinterpret_cast<const float4*>(src);
-        num[0] = fmaf(w, v.x, num[0]);
-        num[1] = fmaf(w, v.y, num[1]);
-        num[2] = fmaf(w, v.z, num[2]);
-        num[3] = fmaf(w, v.w, num[3]);
-      } else {
-        const float2 v = *reinterpret_cast<const float2*>(src);
-        num[0] = fmaf(w, v.x, num[0]);
-        num[1] = fmaf(w, v.y, num[1]);
+    for (int s0 = 0; s0 < ns; s0 += 32) {
+      const int cnt = min(32, ns - s0);
+      float wl = 0.f;
+      if (lane < cnt)
+        wl = lrow[(s0 + lane) * p.ml_part_stride] *
+             fast_exp2(mrow[(s0 + lane) * p.ml_part_stride] - mx);
+      den += wl;
+      for (int t0 = 0; t0 < cnt; t0 += 8) {
+        float v[8][DV];
+        float w[8];
+#pragma unroll
+        for (int u = 0; u < 8; ++u) {
+          const int t = t0 + u;
+          w[u] = __shfl_sync(0xffffffffu, wl, t & 31);
+          const float* src = orow + static_cast<long long>(s0 + t) * p.o_part_stride;
+          if (t < cnt) {
+            if constexpr (DV == 4) {
+              const float4 x = *reinterpret_cast<const float4*>(src);
+              v[u][0] = x.x; v[u][1] = x.y; v[u][2] = x.z; v[u][3] = x.w;
+            } else {
+              const float2 x = *reinterpret_cast<const float2*>(src);
+              v[u][0] = x.x; v[u][1] = x.y;
+            }
+          } else {
+#pragma unroll
+            for (int j = 0; j < DV; ++j) v[u][j] = 0.f;
+            w[u] = 0.f;
+          }
+        }
+#pragma unroll
+        for (int u = 0; u < 8; ++u)
+#pragma unroll
+          for (int j = 0; j < DV; ++j) num[j] = fmaf(w[u], v[u][j], num[j]);
       }
     }
+    den = warp_sum(den);
   }
   const float inv = den > 0.f ? 1.f / den : 0.f;
   if (p.out16 != nullptr) {

@@ -50,9 +50,13 @@ def test_decode_partition_contract():
         assert p % ak.CHUNK == 0 and p >= ak.CHUNK
         splits = -(-ctx // p)
         assert splits <= max(1, -(-ctx // ak.CHUNK))
-    # A small batch is split finely; a big one not at all.
-    assert ak.decode_partition(1, 8, 32768, sm_count=148) == 256
+    # A small batch is split (at most 32 ways); a big one not at all.
+    assert ak.decode_partition(1, 8, 32768, sm_count=148) == 1024
     assert ak.decode_partition(4096, 32, 4096, sm_count=148) == 4096
+    # BASELINE config 4 (64 x 32 heads, ctx up to 8192) lands on its stated 512.
+    assert ak.decode_partition(64, 32, 8192, sm_count=148) == 512
+    # One rank's share of config 5 at 8 GPUs (8 x 32 heads, 16384 tokens): 512.
+    assert ak.decode_partition(8, 32, 16384, sm_count=148) == 512
 
 
 def test_shard_range_partitions():
