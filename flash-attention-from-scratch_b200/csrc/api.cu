@@ -118,9 +118,9 @@ int attn_flash_fwd(const void* q, const void* k, const void* v, void* o, int64_t
     return fail(ATTN_ERR_UNSUPPORTED,
                 "flash_wmma: head_dim must be 64 or 128 and block_n 32 or 64 (got block_n %lld)",
                 static_cast<long long>(block_n));
-  if ((seq + 255) / 256 > 65535)
-    return fail(ATTN_ERR_UNSUPPORTED, "flash_wmma: seq %lld is above 16776960",
-                static_cast<long long>(seq));
+  if ((batch * heads) * ((seq + 255) / 256) > 0x7fffffffLL)
+    return fail(ATTN_ERR_UNSUPPORTED,
+                "flash_wmma: batch * heads * ceil(seq / 256) must fit in 31 bits");
   if (batch * heads == 0 || seq == 0) return ATTN_OK;
   LaunchCtx ctx;
   rc = device_ctx(static_cast<cudaStream_t>(stream), &ctx);

@@ -28,14 +28,16 @@
 //     (P then stays <= 256, well inside fp16); the final O / l uses the same
 //     stale max for numerator and denominator, so the result is unchanged.
 //   * Causal: key tiles after a query tile's diagonal are never loaded or
-//     multiplied; only the diagonal tile is masked element-wise. CTAs are
-//     scheduled longest-first.
+//     multiplied; only the diagonal tile is masked element-wise. CTAs run
+//     longest first inside groups of (batch, head) pairs, so the K/V tiles
+//     of the CTAs in flight stay in L2.
 //
 // TMEM columns (512 allocated): S_0 [0,128), S_1 [128,256), O_0 and O_1 after.
 // Every mbarrier wait is bounded; on timeout the CTA records the failure in
 // the device status word, drains its copies and MMAs, frees TMEM and exits.
 #include <cudaTypedefs.h>
 
+#include <algorithm>
 #include <mutex>
 
 #include "common.cuh"
@@ -123,6 +125,9 @@ struct TcParams {
   int n;            // sequence length
   int n_tiles;      // ceil(n / 128): query tiles = key tiles
   int n_cta_tiles;  // ceil(n_tiles / NQ)
+  int bh;           // batch * heads
+  int group;        // (batch, head) pairs per scheduling group
+  int first_group;  // pairs in the first group (1 .. group; the remainder)
   int causal;
   float scale_log2;
 };
@@ -152,8 +157,27 @@ __global__ void __launch_bounds__(TcCfg<D, NQ>::THREADS, 1)
 
   const int warp = threadIdx.x >> 5;
   const int lane = threadIdx.x & 31;
-  const int bh = blockIdx.x;
-  const int qt0 = (p.n_cta_tiles - 1 - static_cast<int>(blockIdx.y)) * NQ;  // longest first
+  // CTA order: the (batch, head) pairs in groups (the remainder group first,
+  // then groups of p.group); inside a group the CTA rows run longest first
+  // (row y = 0 holds the tiles nearest the end of the sequence), the pairs of
+  // one row next to each other. The CTAs in flight then read the K/V of about
+  // one group of pairs, which stays in L2, and the grid still ends on short
+  // tiles, as a plain longest-first order does.
+  int bh, qt0;
+  {
+    int r = static_cast<int>(blockIdx.x), g0 = 0, g_n = p.first_group;
+    const int first_items = p.first_group * p.n_cta_tiles;
+    if (r >= first_items) {
+      r -= first_items;
+      const int grp = r / (p.group * p.n_cta_tiles);
+      r -= grp * p.group * p.n_cta_tiles;
+      g0 = p.first_group + grp * p.group;
+      g_n = p.group;
+    }
+    const int y = r / g_n;
+    bh = g0 + (r - y * g_n);
+    qt0 = (p.n_cta_tiles - 1 - y) * NQ;
+  }
   const int nkv_max = kv_tiles_of(p, min(qt0 + NQ - 1, p.n_tiles - 1));
 
   if (threadIdx.x == 0) {
@@ -413,9 +437,6 @@ __global__ void __launch_bounds__(TcCfg<D, NQ>::THREADS, 1)
           }
         };
         float mt[8];
-        auto row_max = [&]() {
-          return fmax3(fmax3(mt[0], mt[1], mt[2]), fmax3(mt[3], mt[4], mt[5]), fmaxf(mt[6], mt[7])) * cs;
-        };
         load_row();
 #pragma unroll
         for (int a = 0; a < 8; ++a)
@@ -424,7 +445,9 @@ __global__ void __launch_bounds__(TcCfg<D, NQ>::THREADS, 1)
 #pragma unroll
         for (int c = 24; c < kBN; c += 2)
           mt[(c / 2) & 7] = fmax3(mt[(c / 2) & 7], __uint_as_float(sr[c]), __uint_as_float(sr[c + 1]));
-        const float m_new = fmaxf(m, row_max());
+        const float m_new =
+            fmaxf(m, fmax3(fmax3(mt[0], mt[1], mt[2]), fmax3(mt[3], mt[4], mt[5]),
+                           fmaxf(mt[6], mt[7])) * cs);
         if (j == 0) {
           m = m_new;
         } else if (__any_sync(0xffffffffu, m_new > m + kRescaleThreshold)) {
@@ -555,7 +578,7 @@ cudaError_t launch_tc(const TcParams& prm, int64_t bh, const LaunchCtx& ctx) {
                                     C::SMEM_ALLOC);
   });
   if (attr_err != cudaSuccess) return attr_err;
-  dim3 grid(static_cast<unsigned>(bh), static_cast<unsigned>(prm.n_cta_tiles));
+  const unsigned grid = static_cast<unsigned>(bh * prm.n_cta_tiles);
   kern<<<grid, C::THREADS, C::SMEM_ALLOC, ctx.stream>>>(prm);
   return cudaGetLastError();
 }
@@ -576,6 +599,15 @@ cudaError_t launch_flash_tc(const void* q, const void* k, const void* v, void* o
   prm.n = static_cast<int>(n);
   prm.n_tiles = static_cast<int>((n + kBM - 1) / kBM);
   prm.n_cta_tiles = (prm.n_tiles + kNQ - 1) / kNQ;
+  prm.bh = static_cast<int>(bh);
+  // Pairs per group: enough for about four CTAs per SM, which keeps the
+  // finishing times as even as one longest-first wave (checked by simulating
+  // the greedy block dispatch over batch, head and length mixes).
+  const int64_t want = (4 * static_cast<int64_t>(ctx.sm_count) + prm.n_cta_tiles - 1) /
+                       prm.n_cta_tiles;
+  prm.group = static_cast<int>(std::min<int64_t>(bh, std::max<int64_t>(1, want)));
+  const int64_t n_groups = (bh + prm.group - 1) / prm.group;
+  prm.first_group = static_cast<int>(bh - (n_groups - 1) * prm.group);
   prm.causal = causal ? 1 : 0;
   prm.scale_log2 = scale * kLog2e;
   if (d == 64) return launch_tc<64, kNQ>(prm, bh, ctx);
