@@ -104,11 +104,11 @@ struct TcCfg {
   static constexpr int LOAD_WARP = SOFT_WARPS + 1;
   static constexpr int THREADS = 32 * (SOFT_WARPS + 4);
   // Register split (setmaxnreg): launched at 168 per thread (65536 / 384,
-  // rounded down to 8); the control warpgroup drops to 56 and the softmax
-  // warpgroups rise to 224: 128 * 56 + 256 * 224 = 384 * 168.
+  // rounded down to 8); the control warpgroup drops to 64 and the softmax
+  // warpgroups rise to 216: 128 * 64 + 256 * 216 <= 384 * 168.
   static constexpr int LAUNCH_REGS = 168;
-  static constexpr int CONTROL_REGS = 56;
-  static constexpr int SOFTMAX_REGS = 224;
+  static constexpr int CONTROL_REGS = 64;
+  static constexpr int SOFTMAX_REGS = 216;
   static_assert(NQ == 2, "the register split assumes two softmax warpgroups");
   static_assert(128 * CONTROL_REGS + 256 * SOFTMAX_REGS <= THREADS * LAUNCH_REGS, "register split");
   static constexpr int O_COL = NQ * kBN;  // first O column; S_i at i * kBN
@@ -250,58 +250,82 @@ __global__ void __launch_bounds__(TcCfg<D, NQ>::THREADS, 1)
     }
   } else if (warp == C::MMA_WARP) {
     // ------------------------------------------------------------- MMA issuer
-    if (lane == 0) {
+    // The whole warp runs the issue loop (warp-uniform operands); one elected
+    // lane issues each MMA and commit. Waits are voted so every lane takes the
+    // same path.
+    {
       constexpr uint32_t kIdescS = idesc_f16_f32(kBM, kBN, false, false);
       constexpr uint32_t kIdescO = idesc_f16_f32(kBM, D, false, true);
-      const uint32_t q_base = smem_u32(smem + C::Q_OFF);
-      const uint32_t ring_base = smem_u32(smem + C::RING_OFF);
-      auto item_addr = [&](int it) { return ring_base + (it % C::SLOTS) * C::TILE_BYTES; };
-      auto wait_item = [&](int it) {
-        return mbar_wait(full + it % C::SLOTS, (it / C::SLOTS) & 1, abort_flag, p.status,
-                         (it & 1) ? kSiteMmaV : kSiteMmaK, p.timeout_ns);
+      // Descriptors are built once; a K step or a ring slot moves the start
+      // address field (address / 16, bits 0-13), which never carries out
+      // because shared memory ends below 256 KB.
+      const uint64_t q_desc = sdesc_sw128(smem_u32(smem + C::Q_OFF), 16, 1024);
+      const uint64_t k_desc0 = sdesc_sw128(smem_u32(smem + C::RING_OFF), 16, 1024);
+      const uint64_t v_desc0 = sdesc_sw128(smem_u32(smem + C::RING_OFF), C::BLK_BYTES, 1024);
+      constexpr uint32_t kTileStep = C::TILE_BYTES >> 4;
+      auto wait_slot = [&](int slot, uint32_t phase, unsigned int site) {
+        const bool r = mbar_wait(full + slot, phase, abort_flag, p.status, site, p.timeout_ns);
+        return __all_sync(0xffffffffu, r);
       };
       int nkv[NQ];
 #pragma unroll
       for (int i = 0; i < NQ; ++i) nkv[i] = kv_tiles_of(p, qt0 + i);
 
       // S_i = Q_i K^T: K = D in steps of 16 (32 bytes inside a 128-byte swizzle row).
-      auto issue_s = [&](int i, uint32_t b0) {
-        const uint32_t a0 = q_base + i * C::TILE_BYTES;
+      auto issue_s = [&](int i, int slot) {
+        const uint64_t a0 = q_desc + i * kTileStep;
+        const uint64_t b0 = k_desc0 + static_cast<uint32_t>(slot) * kTileStep;
 #pragma unroll
         for (int kk = 0; kk < D / 16; ++kk) {
-          const uint32_t off = (kk >> 2) * C::BLK_BYTES + (kk & 3) * 32;
-          mma_f16_ss(tmem + i * kBN, sdesc_sw128(a0 + off, 16, 1024),
-                     sdesc_sw128(b0 + off, 16, 1024), kIdescS, kk > 0 ? 1u : 0u);
+          constexpr uint32_t kBlk = C::BLK_BYTES >> 4;
+          const uint32_t off = (kk >> 2) * kBlk + (kk & 3) * 2;
+          mma_f16_ss_warp(tmem + i * kBN, a0 + off, b0 + off, kIdescS, kk > 0 ? 1u : 0u);
         }
       };
       // O_i (+)= P_i V: K = 128 keys in steps of 16 rows (2 KB of V); V is
       // MN-major, the 64-column blocks 16 KB apart (LBO), 8-row groups 1 KB (SBO).
       // Half h covers keys [64 h, 64 h + 64): P columns [32 h, 32 h + 32).
-      auto issue_pv = [&](int i, uint32_t b0, int h, bool accumulate) {
+      auto issue_pv = [&](int i, int slot, int h, bool accumulate) {
+        const uint64_t b0 = v_desc0 + static_cast<uint32_t>(slot) * kTileStep;
 #pragma unroll
         for (int kk = 4 * h; kk < 4 * h + 4; ++kk) {
-          mma_f16_ts(tmem + C::O_COL + i * D, tmem + i * kBN + kk * 8,
-                     sdesc_sw128(b0 + kk * 2048, C::BLK_BYTES, 1024), kIdescO,
-                     (accumulate || kk > 0) ? 1u : 0u);
+          mma_f16_ts_warp(tmem + C::O_COL + i * D, tmem + i * kBN + kk * 8, b0 + kk * (2048 >> 4),
+                          kIdescO, (accumulate || kk > 0) ? 1u : 0u);
         }
       };
 
-      bool ok = mbar_wait(q_full, 0, abort_flag, p.status, kSiteMmaQ, p.timeout_ns) &&
-                wait_item(0);
+      // Ring position of the next item: slot and the parity of its use.
+      int slot = 0;
+      uint32_t phase = 0;
+      auto advance = [&]() {
+        if (++slot == C::SLOTS) {
+          slot = 0;
+          phase ^= 1u;
+        }
+      };
+      bool ok = __all_sync(0xffffffffu,
+                           mbar_wait(q_full, 0, abort_flag, p.status, kSiteMmaQ, p.timeout_ns));
+      ok = ok && wait_slot(0, 0, kSiteMmaK);
       if (ok) {
         tc_fence_after();
 #pragma unroll
         for (int i = 0; i < NQ; ++i) {
           if (nkv[i] > 0) {
-            issue_s(i, item_addr(0));
-            tc_commit(s_full + i);
+            issue_s(i, 0);
+            tc_commit_warp(s_full + i);
           }
         }
-        tc_commit(empty + 0);
+        tc_commit_warp(empty + 0);
       }
+      advance();  // item 1: V_0
       for (int j = 0; ok && j < nkv_max; ++j) {
-        const int v_it = 2 * j + 1, k_it = 2 * j + 2;  // V_j, K_{j+1}
-        ok = wait_item(v_it);
+        const int v_slot = slot;  // V_j
+        const uint32_t v_phase = phase;
+        advance();
+        const int k_slot = slot;  // K_{j+1}
+        const uint32_t k_phase = phase;
+        advance();
+        ok = wait_slot(v_slot, v_phase, kSiteMmaV);
         if (!ok) break;
         tc_fence_after();
         const bool next = j + 1 < nkv_max;
@@ -309,34 +333,35 @@ __global__ void __launch_bounds__(TcCfg<D, NQ>::THREADS, 1)
 #pragma unroll
         for (int i = 0; i < NQ; ++i) {
           if (j < nkv[i]) {
-            ok = mbar_wait(p_full + 2 * i, j & 1, abort_flag, p.status, kSiteMmaP, p.timeout_ns);
+            ok = __all_sync(0xffffffffu, mbar_wait(p_full + 2 * i, j & 1, abort_flag, p.status,
+                                                   kSiteMmaP, p.timeout_ns));
             if (!ok) break;
             tc_fence_after();
-            issue_pv(i, item_addr(v_it), 0, j > 0);
-            ok = mbar_wait(p_full + 2 * i + 1, j & 1, abort_flag, p.status, kSiteMmaP,
-                           p.timeout_ns);
+            issue_pv(i, v_slot, 0, j > 0);
+            ok = __all_sync(0xffffffffu, mbar_wait(p_full + 2 * i + 1, j & 1, abort_flag, p.status,
+                                                   kSiteMmaP, p.timeout_ns));
             if (!ok) break;
             tc_fence_after();
-            issue_pv(i, item_addr(v_it), 1, true);
-            tc_commit(o_full + i);
+            issue_pv(i, v_slot, 1, true);
+            tc_commit_warp(o_full + i);
           }
           if (next && j + 1 < nkv[i]) {
             if (!k_ready) {
-              ok = wait_item(k_it);
+              ok = wait_slot(k_slot, k_phase, kSiteMmaK);
               if (!ok) break;
               tc_fence_after();
               k_ready = true;
             }
-            issue_s(i, item_addr(k_it));
-            tc_commit(s_full + i);
+            issue_s(i, k_slot);
+            tc_commit_warp(s_full + i);
           }
         }
         if (!ok) break;
-        tc_commit(empty + v_it % C::SLOTS);
-        if (next && k_ready) tc_commit(empty + k_it % C::SLOTS);
+        tc_commit_warp(empty + v_slot);
+        if (next && k_ready) tc_commit_warp(empty + k_slot);
       }
       // Every MMA issued completes before tensor memory is released.
-      tc_commit(drain);
+      tc_commit_warp(drain);
       mbar_wait(drain, 0, nullptr, p.status, kSiteDrainMma, p.timeout_ns);
     }
     __syncwarp();
