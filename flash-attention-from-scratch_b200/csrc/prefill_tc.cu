@@ -150,7 +150,7 @@ __global__ void __launch_bounds__(TcCfg<D, NQ>::THREADS, 1)
   uint64_t* empty = full + C::SLOTS;     // ring slot released by the MMAs that read it
   uint64_t* s_full = empty + C::SLOTS;   // MMA -> softmax: S_i ready
   uint64_t* p_full = s_full + NQ;       // softmax -> MMA: half h of P_i written (2 i + h)
-  uint64_t* o_full = p_full + 2 * NQ;   // MMA -> softmax: O_i += P_i V done
+  uint64_t* o_full = p_full + 2 * NQ;   // MMA -> softmax: the last P_i V done
   uint64_t* drain = o_full + NQ;
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(smem + C::MISC_OFF);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(smem + C::MISC_OFF + 4);
@@ -250,9 +250,9 @@ __global__ void __launch_bounds__(TcCfg<D, NQ>::THREADS, 1)
     }
   } else if (warp == C::MMA_WARP) {
     // ------------------------------------------------------------- MMA issuer
-    // The whole warp runs the issue loop (warp-uniform operands); one elected
-    // lane issues each MMA and commit. Waits are voted so every lane takes the
-    // same path.
+    // The whole warp runs the loop and its waits (voted, so every lane takes
+    // the same path) and computes the operands as warp-uniform values; each
+    // group of MMAs and commits is then issued by one elected lane.
     {
       constexpr uint32_t kIdescS = idesc_f16_f32(kBM, kBN, false, false);
       constexpr uint32_t kIdescO = idesc_f16_f32(kBM, D, false, true);
@@ -279,7 +279,7 @@ __global__ void __launch_bounds__(TcCfg<D, NQ>::THREADS, 1)
         for (int kk = 0; kk < D / 16; ++kk) {
           constexpr uint32_t kBlk = C::BLK_BYTES >> 4;
           const uint32_t off = (kk >> 2) * kBlk + (kk & 3) * 2;
-          mma_f16_ss_warp(tmem + i * kBN, a0 + off, b0 + off, kIdescS, kk > 0 ? 1u : 0u);
+          mma_f16_ss(tmem + i * kBN, a0 + off, b0 + off, kIdescS, kk > 0 ? 1u : 0u);
         }
       };
       // O_i (+)= P_i V: K = 128 keys in steps of 16 rows (2 KB of V); V is
@@ -289,8 +289,8 @@ __global__ void __launch_bounds__(TcCfg<D, NQ>::THREADS, 1)
         const uint64_t b0 = v_desc0 + static_cast<uint32_t>(slot) * kTileStep;
 #pragma unroll
         for (int kk = 4 * h; kk < 4 * h + 4; ++kk) {
-          mma_f16_ts_warp(tmem + C::O_COL + i * D, tmem + i * kBN + kk * 8, b0 + kk * (2048 >> 4),
-                          kIdescO, (accumulate || kk > 0) ? 1u : 0u);
+          mma_f16_ts(tmem + C::O_COL + i * D, tmem + i * kBN + kk * 8, b0 + kk * (2048 >> 4),
+                     kIdescO, (accumulate || kk > 0) ? 1u : 0u);
         }
       };
 
@@ -308,14 +308,17 @@ __global__ void __launch_bounds__(TcCfg<D, NQ>::THREADS, 1)
       ok = ok && wait_slot(0, 0, kSiteMmaK);
       if (ok) {
         tc_fence_after();
+        if (elect_one()) {
 #pragma unroll
-        for (int i = 0; i < NQ; ++i) {
-          if (nkv[i] > 0) {
-            issue_s(i, 0);
-            tc_commit_warp(s_full + i);
+          for (int i = 0; i < NQ; ++i) {
+            if (nkv[i] > 0) {
+              issue_s(i, 0);
+              tc_commit(s_full + i);
+            }
           }
+          tc_commit(empty + 0);
         }
-        tc_commit_warp(empty + 0);
+        __syncwarp();
       }
       advance();  // item 1: V_0
       for (int j = 0; ok && j < nkv_max; ++j) {
@@ -325,9 +328,8 @@ __global__ void __launch_bounds__(TcCfg<D, NQ>::THREADS, 1)
         const int k_slot = slot;  // K_{j+1}
         const uint32_t k_phase = phase;
         advance();
-        ok = wait_slot(v_slot, v_phase, kSiteMmaV);
+        ok = wait_slot(v_slot, v_phase, kSiteMmaV);  // (the fence follows the P wait)
         if (!ok) break;
-        tc_fence_after();
         const bool next = j + 1 < nkv_max;
         bool k_ready = false;
 #pragma unroll
@@ -337,31 +339,42 @@ __global__ void __launch_bounds__(TcCfg<D, NQ>::THREADS, 1)
                                                    kSiteMmaP, p.timeout_ns));
             if (!ok) break;
             tc_fence_after();
-            issue_pv(i, v_slot, 0, j > 0);
+            if (elect_one()) issue_pv(i, v_slot, 0, j > 0);
+            __syncwarp();
             ok = __all_sync(0xffffffffu, mbar_wait(p_full + 2 * i + 1, j & 1, abort_flag, p.status,
                                                    kSiteMmaP, p.timeout_ns));
             if (!ok) break;
             tc_fence_after();
-            issue_pv(i, v_slot, 1, true);
-            tc_commit_warp(o_full + i);
-          }
-          if (next && j + 1 < nkv[i]) {
-            if (!k_ready) {
-              ok = wait_slot(k_slot, k_phase, kSiteMmaK);
-              if (!ok) break;
-              tc_fence_after();
-              k_ready = true;
+            if (elect_one()) {
+              issue_pv(i, v_slot, 1, true);
+              if (j + 1 == nkv[i]) tc_commit(o_full + i);  // O_i final
             }
-            issue_s(i, k_slot);
-            tc_commit_warp(s_full + i);
+            __syncwarp();
+            if (next && j + 1 < nkv[i]) {
+              if (!k_ready) {
+                ok = wait_slot(k_slot, k_phase, kSiteMmaK);
+                if (!ok) break;
+                tc_fence_after();
+                k_ready = true;
+              }
+              if (elect_one()) {
+                issue_s(i, k_slot);
+                tc_commit(s_full + i);
+              }
+              __syncwarp();
+            }
           }
         }
         if (!ok) break;
-        tc_commit_warp(empty + v_slot);
-        if (next && k_ready) tc_commit_warp(empty + k_slot);
+        if (elect_one()) {
+          tc_commit(empty + v_slot);
+          if (next && k_ready) tc_commit(empty + k_slot);
+        }
+        __syncwarp();
       }
       // Every MMA issued completes before tensor memory is released.
-      tc_commit_warp(drain);
+      if (elect_one()) tc_commit(drain);
+      __syncwarp();
       mbar_wait(drain, 0, nullptr, p.status, kSiteDrainMma, p.timeout_ns);
     }
     __syncwarp();
@@ -476,13 +489,10 @@ __global__ void __launch_bounds__(TcCfg<D, NQ>::THREADS, 1)
         if (j == 0) {
           m = m_new;
         } else if (__any_sync(0xffffffffu, m_new > m + kRescaleThreshold)) {
-          // Rescale O to the new max; O_i must hold P_{j-1} V first.
+          // Rescale O to the new max. O_i already holds P_{j-1} V: the MMAs of
+          // one thread complete in order, and S_i(j), whose completion this
+          // thread waited for, was issued after P_{j-1} V.
           const float alpha = fast_exp2(m - m_new);
-          ok = mbar_wait(o_full + wg, (j - 1) & 1, abort_flag, p.status, kSiteSoftO,
-                         p.timeout_ns);
-          ok = __all_sync(0xffffffffu, ok);
-          if (!ok) break;
-          tc_fence_after();
 #pragma unroll
           for (int c0 = 0; c0 < D; c0 += 32) {
             uint32_t o[32];
@@ -524,7 +534,7 @@ __global__ void __launch_bounds__(TcCfg<D, NQ>::THREADS, 1)
         }
       }
       if (ok) {
-        ok = mbar_wait(o_full + wg, (n_i - 1) & 1, abort_flag, p.status, kSiteEpilogue,
+        ok = mbar_wait(o_full + wg, 0, abort_flag, p.status, kSiteEpilogue,
                        p.timeout_ns);
         ok = __all_sync(0xffffffffu, ok);
       }
