@@ -10,7 +10,8 @@
 //   * A CTA owns NQ = 2 query tiles of 128 rows of one (batch, head) and walks
 //     the key/value tiles of 128 rows. Warp roles:
 //       warps 0-3, 4-7  softmax warpgroups, one per query tile, one thread per row
-//       warp  8         MMA issuer (one thread) + tensor-memory allocator
+//       warp  8         MMA issuer (the warp runs the loop, one elected lane
+//                       issues) + tensor-memory allocator
 //       warp  9         TMA producer (one thread)
 //       warps 10-11     idle (they complete the control warpgroup)
 //     setmaxnreg moves registers from the control warpgroup to the softmax
@@ -73,7 +74,7 @@ enum : unsigned int {
   kSiteMmaP,
   kSiteDrainMma,
   kSiteSoftS,
-  kSiteSoftO,
+  kSiteSoftO,  // (unused: the rescale needs no wait; kept so site numbers stay stable)
   kSiteEpilogue
 };
 
