@@ -414,6 +414,82 @@ def bench_decode_cfg4(args, d: Dist, peaks, peak_src, traffic):
     return res
 
 
+def torch_comparison(args, d: Dist, ours_prefill, ours_decode):
+    """Library kernels on the same inputs, for context (not the product): torch
+    SDPA backends on prefill config 2, and for decode config 4 the torch route
+    the reference compares against (gather the paged K/V into a contiguous padded
+    cache, then SDPA with a length mask)."""
+    import torch.nn.functional as F
+    from torch.nn.attention import SDPBackend, sdpa_kernel
+
+    steps, warmup = max(3, args.steps // 2), 3
+    out = {"note": "library kernels on the same inputs, for context; value = the same "
+                   "metric as the line above"}
+    c = CFG2
+    shape = (c["batch"], c["heads"], c["seq"], c["head_dim"])
+    gen = torch.Generator(device=d.device).manual_seed(2000)
+    q, k, v = (randn_half(shape, gen, d.device) for _ in range(3))
+    flops = prefill_flops(**c)
+    import attnkernels as ak
+
+    pre = {"ours (headline, after clock spin)": round(ours_prefill, 1)}
+    ours = lambda: ak.flash_attention(q, k, v, causal=True)  # noqa: E731
+    ms = timed(ours, steps, warmup, d) / steps
+    pre["ours"] = round(flops / (ms * 1e-3) / 1e12, 1)
+    for name in ("FLASH_ATTENTION", "EFFICIENT_ATTENTION", "CUDNN_ATTENTION"):
+        key = "sdpa_" + name.split("_")[0].lower()
+        be = getattr(SDPBackend, name, None)
+        if be is None:
+            pre[key] = "unavailable: backend not in this torch"
+            continue
+
+        def fn(be=be):
+            with sdpa_kernel([be]):
+                return F.scaled_dot_product_attention(q, k, v, is_causal=True)
+
+        try:
+            fn()
+            torch.cuda.synchronize(d.device)
+            ms = timed(fn, steps, warmup, d) / steps
+            pre[key] = round(flops / (ms * 1e-3) / 1e12, 1)
+        except Exception as e:  # noqa: BLE001  a backend that does not run here
+            pre[key] = "unavailable: " + str(e).splitlines()[0][:120]
+    out["prefill_cfg2_tflops"] = pre
+    del q, k, v
+
+    c = CFG4
+    g = torch.Generator().manual_seed(4000 + d.rank)
+    ctx = torch.randint(c["ctx_lo"], c["ctx_hi"] + 1, (c["batch"],), generator=g).tolist()
+    kc, vc, tables, lens = synthetic_paged_cache(ctx, c["kv_heads"], c["head_dim"],
+                                                 c["block_size"], 4000 + d.rank, d.device)
+    gq = torch.Generator(device=d.device).manual_seed(4100 + d.rank)
+    qd = randn_half((c["batch"], c["heads"], 1, c["head_dim"]), gq, d.device)
+    nblk = -(-max(ctx) // c["block_size"])
+    idx = torch.arange(nblk * c["block_size"], device=d.device)
+    mask = (idx[None, :] < lens[:, None].long())[:, None, None, :]
+
+    def gather(cache):
+        x = cache[tables[:, :nblk].long()]  # [B, nblk, Hkv, bs, D]
+        return x.permute(0, 2, 1, 3, 4).reshape(x.shape[0], x.shape[2], -1, x.shape[4])
+
+    def gather_sdpa():
+        return F.scaled_dot_product_attention(qd, gather(kc), gather(vc), attn_mask=mask)
+
+    dec = {"ours": round(ours_decode, 1)}
+    try:
+        gather_sdpa()
+        torch.cuda.synchronize(d.device)
+        ms = timed(gather_sdpa, steps, warmup, d) / steps
+        dec["torch_gather_sdpa"] = round(kv_bytes(ctx, c["kv_heads"], c["head_dim"]) /
+                                         (ms * 1e-3) / 1e9, 1)
+    except Exception as e:  # noqa: BLE001
+        dec["torch_gather_sdpa"] = "unavailable: " + str(e).splitlines()[0][:120]
+    out["decode_cfg4_gbps"] = dec
+    del kc, vc, qd, mask
+    torch.cuda.empty_cache()
+    return out
+
+
 def bench_long_context(args, d: Dist, peaks, peak_src):
     """Configs 3 and 5, total work fixed and split over the ranks (strong scaling)."""
     import attnkernels as ak
@@ -619,6 +695,8 @@ def main():
     ap.add_argument("--no-long", action="store_true", help="skip configs 3 and 5")
     ap.add_argument("--no-cpu", action="store_true", help="skip the CPU baseline")
     ap.add_argument("--only-prefill", action="store_true", help="headline kernel only")
+    ap.add_argument("--no-compare", action="store_true",
+                    help="skip the torch SDPA / gather+SDPA comparison rows")
     ap.add_argument("--spin", type=float, default=1.0,
                     help="seconds of untimed load before a timed region (clock sampling)")
     ap.add_argument("--ablation", action="store_true",
@@ -678,6 +756,9 @@ def main():
         line["decode"] = bench_decode_cfg4(args, d, peaks, peak_src, traffic)
         if not args.no_long:
             line["long_context"] = bench_long_context(args, d, peaks, peak_src)
+        if d.world == 1 and not args.no_compare:
+            line["torch_comparison"] = torch_comparison(args, d, line["value"],
+                                                        line["decode"]["value"])
     ak.check_device_status(d.device)
     if d.rank == 0 and d.world == 1 and not args.no_cpu:
         pre_cpu, dec_cpu = cpu_baseline()
