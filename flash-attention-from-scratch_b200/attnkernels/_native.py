@@ -13,6 +13,7 @@ as the reference's TORCH_CHECK does.
 """
 from __future__ import annotations
 
+import contextlib
 import ctypes
 import threading
 from pathlib import Path
@@ -95,6 +96,15 @@ def _stream(device: torch.device):
     return ctypes.c_void_p(torch.cuda.current_stream(device).cuda_stream)
 
 
+def _on(device: torch.device):
+    """Make `device` current for the call (the C ABI works on the current device);
+    no device switch when it already is."""
+    idx = device.index if device.index is not None else torch.cuda.current_device()
+    if torch.cuda.current_device() == idx:
+        return contextlib.nullcontext()
+    return torch.cuda.device(idx)
+
+
 def _workspace(nbytes: int, device: torch.device) -> torch.Tensor:
     # 256-byte aligned: torch's caching allocator aligns every block to >= 512 B.
     return torch.empty(max(int(nbytes), 256), dtype=torch.uint8, device=device)
@@ -110,7 +120,7 @@ class Extension:
     def flash_wmma(self, q, k, v, causal, scale, block_n):
         o = torch.empty_like(q)
         B, H, N, D = q.shape
-        with torch.cuda.device(q.device):
+        with _on(q.device):
             _check(self.lib.attn_flash_fwd(_ptr(q), _ptr(k), _ptr(v), _ptr(o), B, H, N, D,
                                            int(bool(causal)), float(scale), int(block_n),
                                            _stream(q.device)))
@@ -119,7 +129,7 @@ class Extension:
     def flash_simt(self, q, k, v, causal, scale):
         o = torch.empty_like(q)
         B, H, N, D = q.shape
-        with torch.cuda.device(q.device):
+        with _on(q.device):
             _check(self.lib.attn_flash_simt_fwd(_ptr(q), _ptr(k), _ptr(v), _ptr(o), B, H, N, D,
                                                 int(bool(causal)), float(scale),
                                                 _stream(q.device)))
@@ -129,7 +139,7 @@ class Extension:
         o = torch.empty_like(q)
         B, H, N, D = q.shape
         ws = _workspace(self.lib.attn_naive_workspace_bytes(B, H, N), q.device)
-        with torch.cuda.device(q.device):
+        with _on(q.device):
             _check(self.lib.attn_naive_fwd(_ptr(q), _ptr(k), _ptr(v), _ptr(o), B, H, N, D,
                                            int(bool(causal)), float(scale), _ptr(ws),
                                            ws.numel(), _stream(q.device)))
@@ -145,7 +155,7 @@ class Extension:
         B, H, Hkv, D, bs, nblk, maxb = self._decode_sizes(q, kc, bt)
         ws = _workspace(self.lib.attn_paged_decode_workspace_bytes(B, H, D, max_ctx, partition),
                         q.device)
-        with torch.cuda.device(q.device):
+        with _on(q.device):
             _check(self.lib.attn_paged_decode(
                 _ptr(q), _ptr(kc), _ptr(vc), _ptr(bt), _ptr(ctx), _ptr(out), B, H, Hkv, D, bs,
                 nblk, maxb, int(max_ctx), float(scale), int(partition), _ptr(ws), ws.numel(),
@@ -161,7 +171,7 @@ class Extension:
         l = torch.empty(B, H, **f32) if l is None else l
         ws = _workspace(self.lib.attn_paged_decode_workspace_bytes(B, H, D, max_ctx, partition),
                         q.device)
-        with torch.cuda.device(q.device):
+        with _on(q.device):
             _check(self.lib.attn_paged_decode_partials(
                 _ptr(q), _ptr(kc), _ptr(vc), _ptr(bt), _ptr(ctx), _ptr(o), _ptr(m), _ptr(l), B, H,
                 Hkv, D, bs, nblk, maxb, int(max_ctx), float(scale), int(partition), _ptr(ws),
@@ -170,7 +180,7 @@ class Extension:
 
     def merge_partials(self, o_parts, m_parts, l_parts, rows, head_dim, o_part_stride,
                        ml_part_stride, num_parts, out):
-        with torch.cuda.device(out.device):
+        with _on(out.device):
             _check(self.lib.attn_merge_partials(
                 _ptr(o_parts), _ptr(m_parts), _ptr(l_parts), int(num_parts), int(rows),
                 int(head_dim), int(o_part_stride), int(ml_part_stride), _ptr(out),

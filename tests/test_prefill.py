@@ -151,6 +151,25 @@ def test_config3_long_context_rows():
             assert mean_err(o, ref) < MEAN_ABS, (h, r0)
 
 
+@pytest.mark.parametrize("b,h,n", [(3, 100, 384), (2, 97, 1280), (1, 1, 2304)])
+def test_scheduling_groups(b, h, n):
+    """Many (batch, head) pairs: the CTAs run in groups of pairs with a remainder
+    group first. Every pair of every group must be computed exactly once (checked
+    on heads from the first group, a middle one and the last)."""
+    torch.manual_seed(11)
+    q, k, v = rand_qkv(b, h, n, 128)
+    out = ak.flash_attention(q, k, v, causal=True)
+    assert torch.isfinite(out).all()
+    pairs = sorted({0, (b * h) // 2, b * h - 1})
+    for x in pairs:
+        bi, hi = divmod(x, h)
+        ref = oracle(q[bi:bi + 1, hi:hi + 1], k[bi:bi + 1, hi:hi + 1], v[bi:bi + 1, hi:hi + 1], True)
+        o = out[bi:bi + 1, hi:hi + 1]
+        assert max_err(o, ref) < MAX_ABS, (bi, hi)
+        assert mean_err(o, ref) < MEAN_ABS, (bi, hi)
+    ak.check_device_status()
+
+
 @pytest.mark.parametrize("n", [1, 127, 128, 129, 255, 256, 257, 1000])
 @pytest.mark.parametrize("causal", [False, True])
 def test_tile_edges(n, causal):
