@@ -89,10 +89,6 @@ __device__ __forceinline__ bool mbar_test_wait(uint64_t* bar, uint32_t parity) {
   return ok != 0;
 }
 
-#ifndef FAB_WAIT_TEST_FIRST
-#define FAB_WAIT_TEST_FIRST 0
-#endif
-
 // Wait until the phase of `bar` with the given parity has completed, for at
 // most timeout_ns. Returns false (after recording the failure in `st` and
 // raising *abort) on timeout, or at once if *abort is already raised by
@@ -101,7 +97,7 @@ __device__ __forceinline__ bool mbar_test_wait(uint64_t* bar, uint32_t parity) {
 __device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity, volatile int* abort,
                                           DeviceStatus* st, unsigned int site,
                                           unsigned long long timeout_ns) {
-  if (FAB_WAIT_TEST_FIRST ? mbar_test_wait(bar, parity) : mbar_try_wait(bar, parity)) return true;
+  if (mbar_try_wait(bar, parity)) return true;
   const uint64_t t0 = globaltimer_ns();
   for (uint32_t n = 1;; ++n) {
     if (mbar_try_wait(bar, parity)) return true;
