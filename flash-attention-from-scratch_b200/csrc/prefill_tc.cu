@@ -13,7 +13,9 @@
 //       warp  8         MMA issuer (the warp runs the loop, one elected lane
 //                       issues) + tensor-memory allocator
 //       warp  9         TMA producer (one thread)
-//       warps 10-11     idle (they complete the control warpgroup)
+//       warp 10         step signaller: one barrier per key step once V_j and
+//                       K_{j+1} have both arrived, so the MMA warp waits once
+//       warp 11         idle (it completes the control warpgroup)
 //     setmaxnreg moves registers from the control warpgroup to the softmax
 //     warpgroups, so a whole 128-column score row stays in registers.
 //   * Q, K, V tiles arrive by TMA (128-byte swizzle, zero fill past the end of
@@ -96,7 +98,8 @@ struct TcCfg {
   static constexpr int SLOTS_FIT = (227 * 1024 - 1024 - RING_OFF - 512) / TILE_BYTES;
   static constexpr int SLOTS = SLOTS_FIT < 8 ? SLOTS_FIT : 8;
   static constexpr int BAR_OFF = RING_OFF + SLOTS * TILE_BYTES;
-  static constexpr int NUM_BARS = 1 + 2 * SLOTS + 4 * NQ + 1;
+  static constexpr int PAIRS = 4;  // key steps whose V_j + K_{j+1} arrival is signalled ahead
+  static constexpr int NUM_BARS = 1 + 2 * SLOTS + 4 * NQ + 1 + PAIRS;
   static_assert(SLOTS >= 3, "K/V ring");
   static constexpr int MISC_OFF = BAR_OFF + NUM_BARS * 8;
   static constexpr int SMEM_ALLOC = MISC_OFF + 16 + 1024;  // + slack to align the base to 1 KB
@@ -153,6 +156,7 @@ __global__ void __launch_bounds__(TcCfg<D, NQ>::THREADS, 1)
   uint64_t* p_full = s_full + NQ;       // softmax -> MMA: half h of P_i written (2 i + h)
   uint64_t* o_full = p_full + 2 * NQ;   // MMA -> softmax: the last P_i V done
   uint64_t* drain = o_full + NQ;
+  uint64_t* step_full = drain + 1;  // key step j: V_j and K_{j+1} both loaded (j % PAIRS)
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(smem + C::MISC_OFF);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(smem + C::MISC_OFF + 4);
 
@@ -194,6 +198,7 @@ __global__ void __launch_bounds__(TcCfg<D, NQ>::THREADS, 1)
       mbar_init(o_full + i, 1);
     }
     mbar_init(drain, 1);
+    for (int s = 0; s < C::PAIRS; ++s) mbar_init(step_full + s, 1);
     *abort_flag = 0;
     fence_mbar_init();
   }
@@ -249,6 +254,33 @@ __global__ void __launch_bounds__(TcCfg<D, NQ>::THREADS, 1)
           mbar_wait(full + sl, (cnt - 1) & 1, nullptr, p.status, kSiteDrainLoads, p.timeout_ns);
       }
     }
+  } else if (warp == C::MMA_WARP + 2) {
+    // -------------------------------------------------------- step signaller
+    // Folds the two ring waits of a key step into one for the MMA warp: waits
+    // for V_j and then K_{j+1} and arrives on step_full[j % PAIRS]. It runs at
+    // most the ring's depth ahead of the MMAs, fewer key steps than PAIRS.
+    if (lane == 0) {
+      int slot = 1 % C::SLOTS;  // ring item 1: V_0
+      uint32_t phase = 1 / C::SLOTS;
+      auto advance = [&]() {
+        if (++slot == C::SLOTS) {
+          slot = 0;
+          phase ^= 1u;
+        }
+      };
+      for (int j = 0; j < nkv_max; ++j) {
+        if (!mbar_wait(full + slot, phase & 1, abort_flag, p.status, kSiteMmaV, p.timeout_ns))
+          break;
+        advance();
+        if (j + 1 < nkv_max) {
+          if (!mbar_wait(full + slot, phase & 1, abort_flag, p.status, kSiteMmaK, p.timeout_ns))
+            break;
+          advance();
+        }
+        mbar_arrive(step_full + j % C::PAIRS);
+      }
+    }
+    __syncwarp();
   } else if (warp == C::MMA_WARP) {
     // ------------------------------------------------------------- MMA issuer
     // The whole warp runs the loop and its waits (voted, so every lane takes
@@ -329,7 +361,11 @@ __global__ void __launch_bounds__(TcCfg<D, NQ>::THREADS, 1)
         const int k_slot = slot;  // K_{j+1}
         const uint32_t k_phase = phase;
         advance();
-        ok = wait_slot(v_slot, v_phase, kSiteMmaV);  // (the fence follows the P wait)
+        (void)v_phase;
+        (void)k_phase;
+        // V_j and K_{j+1} are loaded (one wait; the fence follows the P wait).
+        ok = __all_sync(0xffffffffu, mbar_wait(step_full + j % C::PAIRS, (j / C::PAIRS) & 1,
+                                               abort_flag, p.status, kSiteMmaV, p.timeout_ns));
         if (!ok) break;
         const bool next = j + 1 < nkv_max;
         bool k_ready = false;
@@ -352,12 +388,7 @@ __global__ void __launch_bounds__(TcCfg<D, NQ>::THREADS, 1)
             }
             __syncwarp();
             if (next && j + 1 < nkv[i]) {
-              if (!k_ready) {
-                ok = wait_slot(k_slot, k_phase, kSiteMmaK);
-                if (!ok) break;
-                tc_fence_after();
-                k_ready = true;
-              }
+              k_ready = true;  // K_{j+1} came with the step signal
               if (elect_one()) {
                 issue_s(i, k_slot);
                 tc_commit(s_full + i);
