@@ -43,6 +43,10 @@ ROOT = Path(__file__).resolve().parent
 sys.path.insert(0, str(ROOT / "flash-attention-from-scratch_b200"))
 sys.path.insert(0, str(ROOT))
 
+# NCCL's own log lines (NCCL_DEBUG=VERSION prints its version) go to stderr, so that
+# stdout carries only the one JSON line; NCCL reads this when it first initialises.
+os.environ.setdefault("NCCL_DEBUG_FILE", "/dev/stderr")
+
 import torch  # noqa: E402
 
 BASELINE_METRIC = "prefill TFLOP/s & paged-decode KV GB/s per B200 at 1/2/4/8 GPUs vs roofline"
