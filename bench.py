@@ -43,8 +43,11 @@ ROOT = Path(__file__).resolve().parent
 sys.path.insert(0, str(ROOT / "flash-attention-from-scratch_b200"))
 sys.path.insert(0, str(ROOT))
 
-# NCCL's own log lines (NCCL_DEBUG=VERSION prints its version) go to stderr, so that
-# stdout carries only the one JSON line; NCCL reads this when it first initialises.
+# stdout carries only the one JSON line: NCCL's version banner (NCCL_DEBUG=VERSION, as
+# the image sets it) is printed to stdout, so that level becomes WARN, and NCCL's log
+# lines go to stderr. NCCL reads both when it first initialises.
+if os.environ.get("NCCL_DEBUG") == "VERSION":
+    os.environ["NCCL_DEBUG"] = "WARN"
 os.environ.setdefault("NCCL_DEBUG_FILE", "/dev/stderr")
 
 import torch  # noqa: E402
