@@ -18,8 +18,10 @@ host buffers, and the CPU oracle timed on this host.
 Timing: W untimed warm-up steps, then exactly K steps between CUDA events on
 the launching stream, with a barrier and a device synchronize on both sides;
 the time is the max over ranks. Inputs are larger than L2 (126 MB) in every
-timed case, so no flush is needed between steps. Data are synthetic (seeded
-N(0, 1) fp16), no dataset is involved.
+timed case, so no flush is needed between steps. SM clocks and clock-event
+reasons are read through NVML every 2 ms during the warm-up and timed steps
+(`clocks` in the line). Data are synthetic (seeded N(0, 1) fp16), no dataset is
+involved.
 
 `--impl reference` times the reference's own CPU implementation of the path
 (its fp32 PyTorch oracle attnkernels/reference.py, restated in oracle/) with all
@@ -197,6 +199,72 @@ class ClockSampler:
                 "reasons": sorted(reasons), "samples": len(sm)}
 
 
+class NvmlClockSampler:
+    """SM clock and clock-event reasons read through NVML every `period_s` on a
+    background thread while the block runs, so that a timed region of a few
+    milliseconds is itself sampled. Falls back to ClockSampler (nvidia-smi every
+    200 ms) when NVML is not usable."""
+
+    # NVML clock-event reason bits (nvml.h: nvmlClocksEventReason*)
+    BITS = {"sw_power_cap": 0x4, "hw_slowdown": 0x8, "sw_thermal_slowdown": 0x20,
+            "hw_thermal_slowdown": 0x40}
+
+    def __init__(self, device: torch.device, period_s=0.002):
+        self.device, self.period = device, period_s
+        self.fallback = None
+        self.sm, self.mx, self.reasons = [], [], set()
+
+    def __enter__(self):
+        import threading
+        try:
+            import pynvml
+            pynvml.nvmlInit()
+            pr = torch.cuda.get_device_properties(self.device)
+            bus = f"{pr.pci_domain_id:08x}:{pr.pci_bus_id:02x}:{pr.pci_device_id:02x}.0"
+            self.nvml = pynvml
+            self.handle = pynvml.nvmlDeviceGetHandleByPciBusId(bus.encode())
+        except Exception:  # noqa: BLE001  no NVML: nvidia-smi sampling instead
+            self.fallback = ClockSampler(self.device.index or 0).__enter__()
+            return self
+        self.stop = threading.Event()
+
+        def run():
+            nv, h = self.nvml, self.handle
+            while not self.stop.is_set():
+                try:
+                    self.sm.append(nv.nvmlDeviceGetClockInfo(h, nv.NVML_CLOCK_SM))
+                    self.mx.append(nv.nvmlDeviceGetMaxClockInfo(h, nv.NVML_CLOCK_SM))
+                    bits = nv.nvmlDeviceGetCurrentClocksEventReasons(h)
+                    self.reasons.update(n for n, b in self.BITS.items() if bits & b)
+                except Exception:  # noqa: BLE001
+                    break
+                self.stop.wait(self.period)
+
+        self.thread = threading.Thread(target=run, daemon=True)
+        self.thread.start()
+        return self
+
+    def __exit__(self, *exc):
+        if self.fallback is not None:
+            return self.fallback.__exit__(*exc)
+        self.stop.set()
+        self.thread.join(timeout=5)
+        try:
+            self.nvml.nvmlShutdown()
+        except Exception:  # noqa: BLE001
+            pass
+        return False
+
+    def summary(self):
+        if self.fallback is not None:
+            return self.fallback.summary()
+        if not self.sm:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": [], "samples": 0}
+        return {"sm_mhz": statistics.median(self.sm), "sm_max_mhz": max(self.mx),
+                "reasons": sorted(self.reasons), "samples": len(self.sm),
+                "source": f"NVML every {self.period * 1e3:.0f} ms during warm-up and timed steps"}
+
+
 def timed(fn, steps, warmup, d: Dist, spin_s=0.0, per_rank=None):
     """ms for exactly `steps` calls of fn (max over ranks), after `warmup` calls.
     If `per_rank` is a list, every rank's own ms is appended to it.
@@ -333,7 +401,7 @@ def bench_prefill_cfg2(args, d: Dist, peaks, peak_src, traffic):
     q, k, v = (randn_half(shape, gen, d.device) for _ in range(3))
     fn = lambda: ak.flash_attention(q, k, v, causal=True)  # noqa: E731
     ranks_ms = []
-    with ClockSampler(d.local) as clk:
+    with NvmlClockSampler(d.device) as clk:
         ms = timed(fn, args.steps, args.warmup, d, spin_s=args.spin, per_rank=ranks_ms)
     flops = prefill_flops(**c)
     res = {
@@ -379,7 +447,7 @@ def bench_decode_cfg4(args, d: Dist, peaks, peak_src, traffic):
     fn = lambda: ak.paged_decode(q, kc, vc, tables, lens, max_ctx,  # noqa: E731
                                  partition_size=c["partition"])
     ranks_ms = []
-    with ClockSampler(d.local) as clk:
+    with NvmlClockSampler(d.device) as clk:
         ms = timed(fn, args.steps, args.warmup, d, spin_s=args.spin, per_rank=ranks_ms)
     nbytes = kv_bytes(ctx, c["kv_heads"], c["head_dim"])
     total_bytes = d.sum(nbytes)  # each rank decodes its own seeded batch
@@ -439,7 +507,7 @@ def torch_comparison(args, d: Dist, ours_prefill, ours_decode):
     flops = prefill_flops(**c)
     import attnkernels as ak
 
-    pre = {"ours (headline, after clock spin)": round(ours_prefill, 1)}
+    pre = {"ours (headline)": round(ours_prefill, 1)}
     ours = lambda: ak.flash_attention(q, k, v, causal=True)  # noqa: E731
     ms = timed(ours, steps, warmup, d) / steps
     pre["ours"] = round(flops / (ms * 1e-3) / 1e12, 1)
@@ -704,8 +772,9 @@ def main():
     ap.add_argument("--only-prefill", action="store_true", help="headline kernel only")
     ap.add_argument("--no-compare", action="store_true",
                     help="skip the torch SDPA / gather+SDPA comparison rows")
-    ap.add_argument("--spin", type=float, default=1.0,
-                    help="seconds of untimed load before a timed region (clock sampling)")
+    ap.add_argument("--spin", type=float, default=0.0,
+                    help="seconds of untimed load before a timed region (default none: the "
+                         "clocks are sampled during the timed steps themselves)")
     ap.add_argument("--ablation", action="store_true",
                     help="print the decode split-size ablation (one JSON list) and exit")
     ap.add_argument("--profile", choices=["prefill", "decode"],
