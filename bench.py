@@ -814,7 +814,7 @@ def main():
         "higher_is_better": True, "scaling": "weak",
         "vs_baseline": round(pre["value"] / d.world / 13.94, 2),
         "vs_baseline_ref": "per GPU vs the reference's flash_wmma_bn32 on the same config on "
-                           "a T4, 13.94 TFLOP/s (BASELINE.md)",
+                           "a T4, 13.94 TFLOP/s (reference results/t4.md:44)",
         "dtype": "fp16", "data": "synthetic",
         "config": {"workload": "causal prefill, BASELINE config 2, one batch per GPU",
                    "batch": CFG2["batch"], "heads": CFG2["heads"], "seq_len": CFG2["seq"],

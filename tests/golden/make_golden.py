@@ -78,7 +78,9 @@ def decode_cases(ref):
 
 
 def main():
-    root = Path(sys.argv[1]) if len(sys.argv) > 1 else Path("/root/reference")
+    if len(sys.argv) < 2:
+        sys.exit("usage: make_golden.py <path to the reference checkout>")
+    root = Path(sys.argv[1])
     ref = load_reference(root)
     torch.set_num_threads(1)  # deterministic reduction order
     prefill_cases(ref)
