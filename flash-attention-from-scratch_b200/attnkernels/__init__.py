@@ -44,8 +44,10 @@ WMMA_BLOCK_N = {64: 64, 128: 64}
 
 # Decode work units (sequence, kv head, split) to aim for per resident warp of
 # the decode kernel, its resident warps per SM, and the most splits of one
-# sequence (each split adds a part to that row's merge). Chosen from the split
-# ablation on B200 (bench.py --ablation).
+# sequence per query head of a kv head (each split adds a part to that row's
+# merge; a unit of G query heads costs about G times the arithmetic per byte, so
+# grouped-query layers get more, shorter units). Chosen from the split ablation
+# on B200 (bench.py --ablation, bench_sweep.py).
 _UNITS_PER_WARP = 32
 _DECODE_WARPS_PER_SM = 8
 _MAX_SPLITS = 32
@@ -98,23 +100,26 @@ def _sm_count(device_index):
     return torch.cuda.get_device_properties(device_index).multi_processor_count
 
 
-def decode_partition(batch, num_kv_heads, max_context_len, device=None, sm_count=None):
+def decode_partition(batch, num_kv_heads, max_context_len, device=None, sm_count=None,
+                     num_heads=None):
     """Tokens per split for paged_decode.
 
     Same contract as attnkernels/__init__.py:93-101 (a multiple of CHUNK, at
     least one chunk per split, more splits when batch * kv heads is small), with
     the B200 target: about _UNITS_PER_WARP (sequence, kv head, split) units per
     resident decode warp (8 per SM), so the persistent kernel balances ragged
-    batches, and at most _MAX_SPLITS splits per sequence, which bounds the merge.
+    batches, and at most _MAX_SPLITS * G splits per sequence, G = num_heads /
+    num_kv_heads (1 when num_heads is not given), which bounds the merge.
     `sm_count` overrides the device query.
     """
     if sm_count is None:
         dev = torch.cuda.current_device() if device is None else device
         sm_count = _sm_count(dev)
+    group = max(1, num_heads // num_kv_heads) if num_heads else 1
     units = max(1, batch * num_kv_heads)
     want = -(-_UNITS_PER_WARP * _DECODE_WARPS_PER_SM * sm_count // units)
     max_chunks = max(1, -(-max_context_len // CHUNK))
-    splits = max(1, min(want, max_chunks, _MAX_SPLITS))
+    splits = max(1, min(want, max_chunks, _MAX_SPLITS * group))
     return -(-max_chunks // splits) * CHUNK
 
 
@@ -141,7 +146,7 @@ def _decode_args(q, k_cache, v_cache, block_tables, context_lens, max_context_le
     scale = 1.0 / math.sqrt(q.shape[-1]) if scale is None else scale
     if partition_size is None:
         partition_size = decode_partition(q3.shape[0], k_cache.shape[1], max_context_len,
-                                          q.device.index)
+                                          q.device.index, num_heads=q3.shape[1])
     partition_size = -(-int(partition_size) // CHUNK) * CHUNK
     return (q3.contiguous(), k_cache.contiguous(), v_cache.contiguous(),
             block_tables.to(device=q.device, dtype=torch.int32).contiguous(),

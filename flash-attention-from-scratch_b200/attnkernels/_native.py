@@ -89,11 +89,19 @@ def _check(rc: int) -> None:
 
 
 def _ptr(t: torch.Tensor | None):
-    return None if t is None else ctypes.c_void_p(t.data_ptr())
+    # ctypes turns a Python int into the c_void_p argument.
+    return None if t is None else t.data_ptr()
+
+
+_raw_stream = getattr(torch._C, "_cuda_getCurrentRawStream", None)
 
 
 def _stream(device: torch.device):
-    return ctypes.c_void_p(torch.cuda.current_stream(device).cuda_stream)
+    """The current CUDA stream of `device` as an integer handle."""
+    idx = device.index if device.index is not None else torch.cuda.current_device()
+    if _raw_stream is not None:
+        return _raw_stream(idx)
+    return torch.cuda.current_stream(idx).cuda_stream
 
 
 def _on(device: torch.device):
@@ -108,6 +116,36 @@ def _on(device: torch.device):
 def _workspace(nbytes: int, device: torch.device) -> torch.Tensor:
     # 256-byte aligned: torch's caching allocator aligns every block to >= 512 B.
     return torch.empty(max(int(nbytes), 256), dtype=torch.uint8, device=device)
+
+
+class _StreamWorkspaces:
+    """One decode scratch buffer per (device, stream), kept between calls and grown
+    when a call needs more, like a BLAS library's workspace: calls on one stream
+    run in order, so each may reuse the bytes of the one before. The buffer is
+    allocated while its stream is current, so the caching allocator never hands
+    its memory to another stream while a kernel may still use it."""
+
+    def __init__(self):
+        self._bufs: dict[tuple[int, int], torch.Tensor] = {}
+        self._lock = threading.Lock()
+
+    def get(self, nbytes: int, device: torch.device, stream: int) -> torch.Tensor:
+        key = (device.index if device.index is not None else torch.cuda.current_device(), stream)
+        buf = self._bufs.get(key)
+        if buf is None or buf.numel() < nbytes:
+            with self._lock:
+                buf = self._bufs.get(key)
+                if buf is None or buf.numel() < nbytes:
+                    buf = _workspace(max(int(nbytes), 1 << 20), device)
+                    self._bufs[key] = buf
+        return buf
+
+    def clear(self) -> None:
+        with self._lock:
+            self._bufs.clear()
+
+
+_decode_ws = _StreamWorkspaces()
 
 
 class Extension:
@@ -153,13 +191,15 @@ class Extension:
     def paged_decode(self, q, kc, vc, bt, ctx, max_ctx, scale, partition):
         out = torch.empty_like(q)
         B, H, Hkv, D, bs, nblk, maxb = self._decode_sizes(q, kc, bt)
-        ws = _workspace(self.lib.attn_paged_decode_workspace_bytes(B, H, D, max_ctx, partition),
-                        q.device)
         with _on(q.device):
+            stream = _stream(q.device)
+            ws = _decode_ws.get(
+                self.lib.attn_paged_decode_workspace_bytes(B, H, D, max_ctx, partition),
+                q.device, stream)
             _check(self.lib.attn_paged_decode(
                 _ptr(q), _ptr(kc), _ptr(vc), _ptr(bt), _ptr(ctx), _ptr(out), B, H, Hkv, D, bs,
                 nblk, maxb, int(max_ctx), float(scale), int(partition), _ptr(ws), ws.numel(),
-                _stream(q.device)))
+                stream))
         return out
 
     def paged_decode_partials(self, q, kc, vc, bt, ctx, max_ctx, scale, partition,
@@ -169,13 +209,15 @@ class Extension:
         o = torch.empty(B, H, D, **f32) if o is None else o
         m = torch.empty(B, H, **f32) if m is None else m
         l = torch.empty(B, H, **f32) if l is None else l
-        ws = _workspace(self.lib.attn_paged_decode_workspace_bytes(B, H, D, max_ctx, partition),
-                        q.device)
         with _on(q.device):
+            stream = _stream(q.device)
+            ws = _decode_ws.get(
+                self.lib.attn_paged_decode_workspace_bytes(B, H, D, max_ctx, partition),
+                q.device, stream)
             _check(self.lib.attn_paged_decode_partials(
                 _ptr(q), _ptr(kc), _ptr(vc), _ptr(bt), _ptr(ctx), _ptr(o), _ptr(m), _ptr(l), B, H,
                 Hkv, D, bs, nblk, maxb, int(max_ctx), float(scale), int(partition), _ptr(ws),
-                ws.numel(), _stream(q.device)))
+                ws.numel(), stream))
         return o, m, l
 
     def merge_partials(self, o_parts, m_parts, l_parts, rows, head_dim, o_part_stride,

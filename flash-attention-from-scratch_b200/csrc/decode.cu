@@ -20,12 +20,14 @@
 //     whole page runs into a per-warp ring of 16-token stages signalled by
 //     mbarriers: a page of one head is bs * D * 2 contiguous bytes (4 KB at
 //     bs = 16, D = 128), so every copy is a long contiguous DRAM burst and
-//     about 190 KB per SM is in flight. The producer runs `STAGES` stages
-//     ahead of the consumer, across unit boundaries.
+//     128 KB of K and V per SM is in flight at D = 128. The producer runs
+//     `STAGES` stages ahead of the consumer, across unit boundaries.
 //   * No tensor cores (one query row per head): scores with 8 lanes per token
 //     and 16-byte shared-memory loads, an online softmax per 16-token stage,
 //     and P V with each lane owning D / 32 output columns. Grouped-query heads
-//     (G = H / H_kv) share every K/V byte.
+//     (G = H / H_kv) share every K/V byte; with G > 1 the partial dots are
+//     reduce-scattered so each lane runs the softmax of one head, and the
+//     probabilities reach P V through a small shared-memory buffer.
 #include <algorithm>
 #include <mutex>
 
@@ -55,7 +57,11 @@ struct DecCfg {
   static constexpr int META_OFF = BAR_OFF + kWarps * STAGES * 8;
   static constexpr int PREFIX_OFF = META_OFF + kWarps * STAGES * 16;
   static constexpr int CTX_OFF = PREFIX_OFF + (kMaxBatch + 1) * 4;
-  static constexpr int SMEM = CTX_OFF + kMaxBatch * 4 + 16;
+  // G > 1: per warp two buffers of the stage's probabilities P [kTok][G] and
+  // rescale factors alpha [G] (fp32), read back as broadcasts by every lane.
+  static constexpr int PBUF = ((kTok + 1) * G * 4 + 15) / 16 * 16;
+  static constexpr int P_OFF = (CTX_OFF + kMaxBatch * 4 + 15) / 16 * 16;
+  static constexpr int SMEM = P_OFF + (G > 1 ? kWarps * 2 * PBUF : 0) + 16;
   static constexpr int E = D / 8;    // K elements per lane in the score phase
   static constexpr int DV = D / 32;  // output columns per lane
   static_assert(STAGES >= 2, "ring needs two stages");
@@ -82,6 +88,46 @@ struct DecParams {
   float scale_log2;
 };
 
+
+// Sums N partial values over the 8 lanes of a token group (lane bits 4, 2, 1 of
+// l8) and scatters them: the lane returns the full sum of value l8 >> (3 - log2 N).
+// N - 1 shuffles instead of 3 N for N separate butterflies.
+template <int N>
+__device__ __forceinline__ float scatter_sum8(const float (&v)[N], int l8) {
+  static_assert(N == 2 || N == 4 || N == 8, "two to eight values");
+  constexpr int H1 = N / 2;
+  const bool b2 = (l8 & 4) != 0;
+  float w[H1];
+#pragma unroll
+  for (int i = 0; i < H1; ++i) {  // w[i]: value (b2 ? H1 : 0) + i over lanes {l, l ^ 4}
+    const float send = b2 ? v[i] : v[H1 + i];
+    const float keep = b2 ? v[H1 + i] : v[i];
+    w[i] = keep + __shfl_xor_sync(0xffffffffu, send, 4);
+  }
+  if constexpr (N == 2) {
+    float x = w[0];
+    x += __shfl_xor_sync(0xffffffffu, x, 2);
+    return x + __shfl_xor_sync(0xffffffffu, x, 1);
+  } else {
+    constexpr int H2 = N / 4;
+    const bool b1 = (l8 & 2) != 0;
+    float u[H2];
+#pragma unroll
+    for (int i = 0; i < H2; ++i) {
+      const float send = b1 ? w[i] : w[H2 + i];
+      const float keep = b1 ? w[H2 + i] : w[i];
+      u[i] = keep + __shfl_xor_sync(0xffffffffu, send, 2);
+    }
+    if constexpr (N == 4) {
+      return u[0] + __shfl_xor_sync(0xffffffffu, u[0], 1);
+    } else {
+      const bool b0 = (l8 & 1) != 0;
+      const float send = b0 ? u[0] : u[1];
+      const float keep = b0 ? u[1] : u[0];
+      return keep + __shfl_xor_sync(0xffffffffu, send, 1);
+    }
+  }
+}
 
 template <int D, int G>
 __global__ void __launch_bounds__(kThreads, 1) paged_decode_kernel(const DecParams p) {
@@ -170,7 +216,7 @@ __global__ void __launch_bounds__(kThreads, 1) paged_decode_kernel(const DecPara
     pst = 0;
     pnst = (pend - pstart + kTok - 1) / kTok;
     bt_base = -(1 << 30);
-    if (lane == 0) nxt = atomicAdd(p.counter, 1u);
+    if (lane == 0) nxt = kWarps * gridDim.x + atomicAdd(p.counter, 1u);
   };
 
   // Issue the copies of the producer's next stage into its ring slot.
@@ -226,10 +272,174 @@ __global__ void __launch_bounds__(kThreads, 1) paged_decode_kernel(const DecPara
   // G <= 2 two accumulator sets (even / odd tokens) halve the FMA chains.
   constexpr int NACC = G <= 2 ? 2 : 1;
   uint64_t acc[NACC][G][C::DV / 2];
+  // G > 1: after the reduce-scatter each lane holds the scores of one head
+  // (hown) and that head's running max and sum; the accumulators pair two heads
+  // per column, (head 2i, head 2i + 1) for column lane * DV + j, so the packed
+  // FMA takes the two heads' probabilities straight from shared memory.
+  constexpr int LG = G == 1 ? 0 : (G == 2 ? 1 : (G == 4 ? 2 : 3));
+  constexpr int HP = G > 1 ? G / 2 : 1;
+  const int hown = l8 >> (3 - LG);
+  const bool p_writer = (l8 & ((8 >> LG) - 1)) == 0;
+  float* pbuf = reinterpret_cast<float*>(smem + C::P_OFF) + warp * 2 * (C::PBUF / 4);
+  float m_own = -INFINITY, l_own = 0.f;
+  uint64_t acc2[NACC][HP][C::DV];
 
   auto half2_pair = [](uint32_t h2) {
     const float2 f = __half22float2(*reinterpret_cast<const __half2*>(&h2));
     return f2_pack(f.x, f.y);
+  };
+
+  // One stage of a unit with G > 1 query heads per kv head (st: the stage's
+  // ring slot, nt: its tokens, md: its unit and flags).
+  auto consume_grouped = [&](const uint8_t* st, int nt, const int4 md) {
+   if constexpr (G > 1) {
+    // Scores: token 4 * step + grp, 8 lanes per token; the G partial dots of a
+    // lane are summed over its token's 8 lanes and scattered, one head per lane.
+    float s1[kTok / 4];
+    const __half* kst = reinterpret_cast<const __half*>(st);
+#pragma unroll
+    for (int step = 0; step < kTok / 4; ++step) {
+      const int t = step * 4 + grp;
+      uint64_t kf[C::E / 2];
+#pragma unroll
+      for (int e8 = 0; e8 < C::E / 8; ++e8) {
+        const uint4 raw = *reinterpret_cast<const uint4*>(kst + t * D + e8 * 64 + l8 * 8);
+        kf[e8 * 4 + 0] = half2_pair(raw.x);
+        kf[e8 * 4 + 1] = half2_pair(raw.y);
+        kf[e8 * 4 + 2] = half2_pair(raw.z);
+        kf[e8 * 4 + 3] = half2_pair(raw.w);
+      }
+      float dot[G];
+#pragma unroll
+      for (int g = 0; g < G; ++g) {
+        uint64_t d0 = f2_mul(qf[g][0], kf[0]);
+        uint64_t d1 = f2_mul(qf[g][1], kf[1]);
+#pragma unroll
+        for (int e = 2; e < C::E / 2; e += 2) {
+          d0 = f2_fma(qf[g][e], kf[e], d0);
+          d1 = f2_fma(qf[g][e + 1], kf[e + 1], d1);
+        }
+        float a, b;
+        f2_unpack(f2_add(d0, d1), a, b);
+        dot[g] = a + b;
+      }
+      const float v = scatter_sum8<G>(dot, l8);
+      s1[step] = (t < nt) ? v : -INFINITY;
+    }
+    // Online softmax of this lane's head over the stage's 16 tokens (4 token groups).
+    float mx = fmaxf(fmaxf(s1[0], s1[1]), fmaxf(s1[2], s1[3]));
+    mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, 8));
+    mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, 16));
+    const float mn = fmaxf(m_own, mx);
+    const float alpha = fast_exp2(m_own - mn);
+    float ps = 0.f;
+#pragma unroll
+    for (int step = 0; step < kTok / 4; ++step) {
+      s1[step] = fast_exp2(s1[step] - mn);
+      ps += s1[step];
+    }
+    ps += __shfl_xor_sync(0xffffffffu, ps, 8);
+    ps += __shfl_xor_sync(0xffffffffu, ps, 16);
+    l_own = l_own * alpha + ps;
+    m_own = mn;
+    // P [token][head] and alpha [head] to this stage's buffer (two alternate, so a
+    // lane that runs ahead never overwrites what another still reads).
+    float* pb = pbuf + (c_item & 1u) * (C::PBUF / 4);
+    if (p_writer) {
+#pragma unroll
+      for (int step = 0; step < kTok / 4; ++step) pb[(step * 4 + grp) * G + hown] = s1[step];
+      if (grp == 0) pb[kTok * G + hown] = alpha;
+    }
+    __syncwarp();
+    const uint64_t* al = reinterpret_cast<const uint64_t*>(pb + kTok * G);
+#pragma unroll
+    for (int i = 0; i < HP; ++i) {
+      const uint64_t a2 = al[i];
+#pragma unroll
+      for (int a = 0; a < NACC; ++a)
+#pragma unroll
+        for (int j = 0; j < C::DV; ++j) acc2[a][i][j] = f2_mul(acc2[a][i][j], a2);
+    }
+    // P V: lane owns columns [lane * DV, lane * DV + DV) of every head. A partial
+    // stage skips the missing tokens, whose shared-memory rows hold stale data.
+    const __half* vst = reinterpret_cast<const __half*>(st + C::KV) + lane * C::DV;
+    auto pv = [&](int t) {
+      float vf[C::DV];
+      if constexpr (C::DV == 4) {
+        const uint2 raw = *reinterpret_cast<const uint2*>(vst + t * D);
+        const float2 x = __half22float2(*reinterpret_cast<const __half2*>(&raw.x));
+        const float2 y = __half22float2(*reinterpret_cast<const __half2*>(&raw.y));
+        vf[0] = x.x; vf[1] = x.y; vf[2] = y.x; vf[3] = y.y;
+      } else {
+        const uint32_t raw = *reinterpret_cast<const uint32_t*>(vst + t * D);
+        const float2 x = __half22float2(*reinterpret_cast<const __half2*>(&raw));
+        vf[0] = x.x; vf[1] = x.y;
+      }
+      const uint64_t* pp = reinterpret_cast<const uint64_t*>(pb + t * G);
+      uint64_t pr[HP];
+#pragma unroll
+      for (int i = 0; i < HP; ++i) pr[i] = pp[i];
+#pragma unroll
+      for (int j = 0; j < C::DV; ++j) {
+        const uint64_t vv = f2_pack(vf[j], vf[j]);
+#pragma unroll
+        for (int i = 0; i < HP; ++i) acc2[t % NACC][i][j] = f2_fma(pr[i], vv, acc2[t % NACC][i][j]);
+      }
+    };
+    if (nt == kTok) {
+#pragma unroll
+      for (int t = 0; t < kTok; ++t) pv(t);
+    } else {
+#pragma unroll
+      for (int t = 0; t < kTok; ++t)
+        if (t < nt) pv(t);
+    }
+    __syncwarp();
+    if (md.w & 64) {
+      const int b = md.x, kvh = md.y, split = md.z;
+      const int ns = min((ctx_s[b] + p.partition - 1) / p.partition, p.num_splits);
+      float o[G][C::DV];
+#pragma unroll
+      for (int i = 0; i < HP; ++i)
+#pragma unroll
+        for (int j = 0; j < C::DV; ++j) {
+          uint64_t v = acc2[0][i][j];
+          if constexpr (NACC == 2) v = f2_add(v, acc2[1][i][j]);
+          f2_unpack(v, o[2 * i][j], o[2 * i + 1][j]);
+        }
+#pragma unroll
+      for (int g = 0; g < G; ++g) {
+        const int src = g << (3 - LG);  // a lane of token group 0 that holds head g
+        const float lg = __shfl_sync(0xffffffffu, l_own, src);
+        const float mg = __shfl_sync(0xffffffffu, m_own, src);
+        const float inv = 1.f / lg;
+#pragma unroll
+        for (int j = 0; j < C::DV; ++j) o[g][j] *= inv;
+        const size_t row = static_cast<size_t>(b) * p.hq + kvh * G + g;
+        if (p.direct_out && ns == 1) {
+          __half* dst = p.out + row * D + lane * C::DV;
+          if constexpr (C::DV == 4) {
+            *reinterpret_cast<uint2*>(dst) =
+                make_uint2(pack_half2(o[g][0], o[g][1]), pack_half2(o[g][2], o[g][3]));
+          } else {
+            *reinterpret_cast<uint32_t*>(dst) = pack_half2(o[g][0], o[g][1]);
+          }
+        } else {
+          const size_t pr = row * p.num_splits + split;
+          float* dst = p.o_part + pr * D + lane * C::DV;
+          if constexpr (C::DV == 4) {
+            *reinterpret_cast<float4*>(dst) = make_float4(o[g][0], o[g][1], o[g][2], o[g][3]);
+          } else {
+            *reinterpret_cast<float2*>(dst) = make_float2(o[g][0], o[g][1]);
+          }
+          if (lane == 0) {
+            p.m_part[pr] = mg;
+            p.l_part[pr] = lg;
+          }
+        }
+      }
+    }
+   }
   };
 
   auto consume = [&]() -> bool {
@@ -261,7 +471,18 @@ __global__ void __launch_bounds__(kThreads, 1) paged_decode_kernel(const DecPara
 #pragma unroll
           for (int j = 0; j < C::DV / 2; ++j) acc[a][g][j] = f2_pack(0.f, 0.f);
       }
+      m_own = -INFINITY;
+      l_own = 0.f;
+#pragma unroll
+      for (int a = 0; a < NACC; ++a)
+#pragma unroll
+        for (int i = 0; i < HP; ++i)
+#pragma unroll
+          for (int j = 0; j < C::DV; ++j) acc2[a][i][j] = f2_pack(0.f, 0.f);
     }
+    if constexpr (G > 1) {
+      consume_grouped(st, nt, md);
+    } else {
     // Scores: token 4 * step + grp, 8 lanes per token, two FMA chains per head.
     float s[kTok / 4][G];
     const __half* kst = reinterpret_cast<const __half*>(st);
@@ -390,11 +611,14 @@ __global__ void __launch_bounds__(kThreads, 1) paged_decode_kernel(const DecPara
         }
       }
     }
+    }  // G == 1
     ++c_item;
     return true;
   };
 
-  if (lane == 0) nxt = atomicAdd(p.counter, 1u);
+  // First unit: warp w of CTA c takes unit w * grid + c, so a launch with fewer
+  // units than warps spreads them over all SMs; later units come from the counter.
+  nxt = warp * gridDim.x + blockIdx.x;
   advance();
   for (int i = 0; i < C::STAGES; ++i) produce();
   while (c_item < p_item) {
@@ -428,69 +652,97 @@ struct MergeParams {
   float* out_l;
 };
 
-// One warp per row; lane owns D / 32 consecutive columns.
-template <int D>
+// WPR warps per row (1 or 8): a CTA of 8 warps merges 8 / WPR rows, and the
+// warps of one row take contiguous ranges of its parts. Lane owns D / 32
+// consecutive columns. With many parts per row (a long context cut into many
+// splits, few rows) eight warps keep eight times as many part rows in flight.
+template <int D, int WPR>
 __global__ void __launch_bounds__(256) merge_partials_kernel(const MergeParams p) {
   constexpr int DV = D / 32;
-  const long long row = static_cast<long long>(blockIdx.x) * 8 + (threadIdx.x >> 5);
+  constexpr int ROWS = 8 / WPR;
+  const int warp = threadIdx.x >> 5;
   const int lane = threadIdx.x & 31;
-  if (row >= p.rows) return;
+  const int sub = warp % WPR;
+  const long long row = static_cast<long long>(blockIdx.x) * ROWS + warp / WPR;
+  bool live = row < p.rows;
   int ns = p.num_parts;
-  if (p.ctx != nullptr) {
+  if (live && p.ctx != nullptr) {
     const int c = max(p.ctx[row / p.hq], 0);
     ns = min((c + p.partition - 1) / p.partition, p.num_parts);
   }
-  if (p.skip_single && ns == 1) return;
-  const float* mrow = p.m + row * p.ml_row_stride;
-  const float* lrow = p.l + row * p.ml_row_stride;
+  if (live && p.skip_single && ns == 1) live = false;
+  if constexpr (WPR == 1) {
+    if (!live) return;
+  }
   float mx = -INFINITY;
-  for (int s = lane; s < ns; s += 32) mx = fmaxf(mx, mrow[s * p.ml_part_stride]);
-  mx = warp_max(mx);
   float num[DV];
 #pragma unroll
   for (int j = 0; j < DV; ++j) num[j] = 0.f;
   float den = 0.f;
-  if (mx != -INFINITY) {
-    // Parts in groups of 32: lane s holds the weight of part s0 + s; the
-    // weights are broadcast by shuffles while eight part rows are loaded at
-    // once, so the loads of a row's parts overlap instead of forming a chain.
-    const float* orow = p.o + row * p.o_row_stride + lane * DV;
-    for (int s0 = 0; s0 < ns; s0 += 32) {
-      const int cnt = min(32, ns - s0);
-      float wl = 0.f;
-      if (lane < cnt)
-        wl = lrow[(s0 + lane) * p.ml_part_stride] *
-             fast_exp2(mrow[(s0 + lane) * p.ml_part_stride] - mx);
-      den += wl;
-      for (int t0 = 0; t0 < cnt; t0 += 8) {
-        float v[8][DV];
-        float w[8];
+  if (live) {
+    const float* mrow = p.m + row * p.ml_row_stride;
+    const float* lrow = p.l + row * p.ml_row_stride;
+    for (int s = lane; s < ns; s += 32) mx = fmaxf(mx, mrow[s * p.ml_part_stride]);
+    mx = warp_max(mx);
+    const int per = (ns + WPR - 1) / WPR;
+    const int s_begin = min(ns, sub * per);
+    const int s_end = min(ns, s_begin + per);
+    if (mx != -INFINITY) {
+      // Parts in groups of 32: lane s holds the weight of part s0 + s; the
+      // weights are broadcast by shuffles while eight part rows are loaded at
+      // once, so the loads of a row's parts overlap instead of forming a chain.
+      const float* orow = p.o + row * p.o_row_stride + lane * DV;
+      for (int s0 = s_begin; s0 < s_end; s0 += 32) {
+        const int cnt = min(32, s_end - s0);
+        float wl = 0.f;
+        if (lane < cnt)
+          wl = lrow[(s0 + lane) * p.ml_part_stride] *
+               fast_exp2(mrow[(s0 + lane) * p.ml_part_stride] - mx);
+        den += wl;
+        for (int t0 = 0; t0 < cnt; t0 += 8) {
+          float v[8][DV];
+          float w[8];
 #pragma unroll
-        for (int u = 0; u < 8; ++u) {
-          const int t = t0 + u;
-          w[u] = __shfl_sync(0xffffffffu, wl, t & 31);
-          const float* src = orow + static_cast<long long>(s0 + t) * p.o_part_stride;
-          if (t < cnt) {
-            if constexpr (DV == 4) {
-              const float4 x = *reinterpret_cast<const float4*>(src);
-              v[u][0] = x.x; v[u][1] = x.y; v[u][2] = x.z; v[u][3] = x.w;
+          for (int u = 0; u < 8; ++u) {
+            const int t = t0 + u;
+            w[u] = __shfl_sync(0xffffffffu, wl, t & 31);
+            const float* src = orow + static_cast<long long>(s0 + t) * p.o_part_stride;
+            if (t < cnt) {
+              if constexpr (DV == 4) {
+                const float4 x = *reinterpret_cast<const float4*>(src);
+                v[u][0] = x.x; v[u][1] = x.y; v[u][2] = x.z; v[u][3] = x.w;
+              } else {
+                const float2 x = *reinterpret_cast<const float2*>(src);
+                v[u][0] = x.x; v[u][1] = x.y;
+              }
             } else {
-              const float2 x = *reinterpret_cast<const float2*>(src);
-              v[u][0] = x.x; v[u][1] = x.y;
+#pragma unroll
+              for (int j = 0; j < DV; ++j) v[u][j] = 0.f;
+              w[u] = 0.f;
             }
-          } else {
-#pragma unroll
-            for (int j = 0; j < DV; ++j) v[u][j] = 0.f;
-            w[u] = 0.f;
           }
+#pragma unroll
+          for (int u = 0; u < 8; ++u)
+#pragma unroll
+            for (int j = 0; j < DV; ++j) num[j] = fmaf(w[u], v[u][j], num[j]);
         }
-#pragma unroll
-        for (int u = 0; u < 8; ++u)
-#pragma unroll
-          for (int j = 0; j < DV; ++j) num[j] = fmaf(w[u], v[u][j], num[j]);
       }
+      den = warp_sum(den);
     }
-    den = warp_sum(den);
+  }
+  if constexpr (WPR > 1) {
+    // The row's warps add their sums in shared memory; the first one writes.
+    __shared__ float red[8][D + 1];
+#pragma unroll
+    for (int j = 0; j < DV; ++j) red[warp][lane * DV + j] = num[j];
+    if (lane == 0) red[warp][D] = den;
+    __syncthreads();
+    if (!live || sub != 0) return;
+    for (int w = 1; w < WPR; ++w) {
+#pragma unroll
+      for (int j = 0; j < DV; ++j) num[j] += red[warp + w][lane * DV + j];
+      den += red[warp + w][D];
+    }
   }
   const float inv = den > 0.f ? 1.f / den : 0.f;
   if (p.out16 != nullptr) {
@@ -568,8 +820,8 @@ cudaError_t launch_decode_kernel(const DecParams& prm, int64_t upper_units, cons
     attr_err = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, C::SMEM);
   });
   if (attr_err != cudaSuccess) return attr_err;
-  const int64_t want = (upper_units + kWarps - 1) / kWarps;
-  const int grid = static_cast<int>(std::max<int64_t>(1, std::min<int64_t>(ctx.sm_count, want)));
+  // One CTA per SM, or one per unit when there are fewer units than SMs.
+  const int grid = static_cast<int>(std::max<int64_t>(1, std::min<int64_t>(ctx.sm_count, upper_units)));
   kern<<<grid, kThreads, C::SMEM, ctx.stream>>>(prm);
   return cudaGetLastError();
 }
@@ -587,11 +839,20 @@ cudaError_t dispatch_group(int g, const DecParams& prm, int64_t upper, const Lau
 
 cudaError_t launch_merge_impl(const MergeParams& mp, int d, cudaStream_t stream) {
   if (mp.rows == 0) return cudaSuccess;
-  const unsigned grid = static_cast<unsigned>((mp.rows + 7) / 8);
-  if (d == 64)
-    merge_partials_kernel<64><<<grid, 256, 0, stream>>>(mp);
-  else
-    merge_partials_kernel<128><<<grid, 256, 0, stream>>>(mp);
+  // Eight warps per row from 32 parts up (at least four parts per warp).
+  if (mp.num_parts >= 32) {
+    const unsigned grid = static_cast<unsigned>(mp.rows);
+    if (d == 64)
+      merge_partials_kernel<64, 8><<<grid, 256, 0, stream>>>(mp);
+    else
+      merge_partials_kernel<128, 8><<<grid, 256, 0, stream>>>(mp);
+  } else {
+    const unsigned grid = static_cast<unsigned>((mp.rows + 7) / 8);
+    if (d == 64)
+      merge_partials_kernel<64, 1><<<grid, 256, 0, stream>>>(mp);
+    else
+      merge_partials_kernel<128, 1><<<grid, 256, 0, stream>>>(mp);
+  }
   return cudaGetLastError();
 }
 

@@ -52,6 +52,9 @@ def test_decode_partition_contract():
         assert splits <= max(1, -(-ctx // ak.CHUNK))
     # A small batch is split (at most 32 ways); a big one not at all.
     assert ak.decode_partition(1, 8, 32768, sm_count=148) == 1024
+    # Grouped-query layers (G query heads per kv head) allow G times as many splits.
+    assert ak.decode_partition(1, 8, 32768, sm_count=148, num_heads=32) == 256
+    assert ak.decode_partition(1, 32, 32768, sm_count=148, num_heads=32) == 1024
     assert ak.decode_partition(4096, 32, 4096, sm_count=148) == 4096
     # BASELINE config 4 (64 x 32 heads, ctx up to 8192) lands on its stated 512.
     assert ak.decode_partition(64, 32, 8192, sm_count=148) == 512

@@ -219,3 +219,39 @@ def test_out_of_range_block_id_is_reported():
     code, _ = ak.device_status()
     assert code == 2
     ak.check_device_status()  # cleared
+
+
+@pytest.mark.parametrize("d", [64, 128])
+@pytest.mark.parametrize("heads", [(8, 4), (32, 8), (16, 2)])
+@pytest.mark.parametrize("partition", [None, 256])
+def test_grouped_heads_at_tolerance(d, heads, partition):
+    """Query heads sharing a kv head (G = 2, 4, 8), ragged contexts, this build's tolerance."""
+    mx, mean = run([3000, 17, 1100, 256, 5], heads[0], heads[1], d, partition=partition)
+    assert mx < MAX_ABS and mean < MEAN_ABS
+
+
+@pytest.mark.parametrize("heads", [(8, 8), (32, 8)])
+def test_many_parts_per_row(heads):
+    """36 splits of a 9000-token context next to rows of 2 and 1 splits: the merge
+    with eight warps per row (32 parts and more), in both output forms."""
+    ctx = [9000, 300, 200]
+    k_cache, v_cache, tables, lens = cache(ctx, heads[1], 128)
+    q = torch.randn(len(ctx), heads[0], 128, device="cuda").half()
+    ref = oracle(q, k_cache, v_cache, tables, lens)
+    out = ak.paged_decode(q, k_cache, v_cache, tables, lens, 9000, partition_size=256)
+    assert max_err(out, ref) < MAX_ABS and mean_err(out, ref) < MEAN_ABS
+    o, m, l = ak.paged_decode_partials(q, k_cache, v_cache, tables, lens, 9000,
+                                       partition_size=256)
+    assert max_err(o, ref) < MAX_ABS and mean_err(o, ref) < MEAN_ABS
+    assert torch.isfinite(m).all() and (l >= 1).all()
+
+
+def test_batch_beyond_one_launch():
+    """More sequences than one launch takes (2048): the batch runs as several launches."""
+    g = torch.Generator().manual_seed(5)
+    ctx = torch.randint(1, 40, (2100,), generator=g).tolist()
+    k_cache, v_cache, tables, lens = cache(ctx, 2, 64, seed=5)
+    q = torch.randn(len(ctx), 8, 64, device="cuda").half()
+    out = ak.paged_decode(q, k_cache, v_cache, tables, lens, max(ctx))
+    ref = oracle(q, k_cache, v_cache, tables, lens)
+    assert max_err(out, ref) < MAX_ABS and mean_err(out, ref) < MEAN_ABS
