@@ -53,6 +53,12 @@ _DECODE_WARPS_PER_SM = 8
 _MAX_SPLITS = 32
 
 
+def _decode_warps_per_sm(group):
+    """Warps per CTA (one CTA per SM) of the decode kernel for G query heads per kv
+    head: 12 for G = 2 and 4, else 8 (DecCfg in csrc/decode.cu)."""
+    return 12 if group in (2, 4) else 8
+
+
 @functools.lru_cache(maxsize=None)
 def load_extension():
     """The native kernels, with the reference extension's call surface."""
@@ -116,11 +122,36 @@ def decode_partition(batch, num_kv_heads, max_context_len, device=None, sm_count
         dev = torch.cuda.current_device() if device is None else device
         sm_count = _sm_count(dev)
     group = max(1, num_heads // num_kv_heads) if num_heads else 1
-    units = max(1, batch * num_kv_heads)
-    want = -(-_UNITS_PER_WARP * _DECODE_WARPS_PER_SM * sm_count // units)
+    return _partition(int(batch), int(num_kv_heads), int(max_context_len), int(sm_count),
+                      group)
+
+
+@functools.lru_cache(maxsize=4096)
+def _partition(batch, num_kv_heads, max_context_len, sm_count, group):
+    seqs = max(1, batch * num_kv_heads)
+    want = -(-_UNITS_PER_WARP * _DECODE_WARPS_PER_SM * sm_count // seqs)
     max_chunks = max(1, -(-max_context_len // CHUNK))
-    splits = max(1, min(want, max_chunks, _MAX_SPLITS * group))
-    return -(-max_chunks // splits) * CHUNK
+    cap = _MAX_SPLITS * group
+    splits = max(1, min(want, max_chunks, cap))
+    part = -(-max_chunks // splits) * CHUNK
+    warps = _decode_warps_per_sm(group) * sm_count
+    if seqs * -(-max_context_len // part) >= 4 * warps:
+        return part
+    # Few units for the resident warps: the launch takes about (rounds of units per
+    # warp) x (tokens per unit); among partitions of 2^k chunks take the largest of
+    # the least such time (fewer parts to merge, whole rounds of warps).
+    best_t, best_p = None, part
+    p = CHUNK
+    while True:
+        s = -(-max_context_len // p)
+        if s <= cap:
+            t = -(-seqs * s // warps) * p
+            if best_t is None or t <= best_t:
+                best_t, best_p = t, p
+        if s <= 1:
+            break
+        p *= 2
+    return best_p
 
 
 def _check_decode(q, k_cache, v_cache):

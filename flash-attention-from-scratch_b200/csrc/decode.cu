@@ -37,31 +37,37 @@
 namespace fab {
 namespace {
 
-constexpr int kTok = 16;       // tokens per pipeline stage
-constexpr int kWarps = 8;      // warps per CTA
-constexpr int kThreads = kWarps * 32;
-constexpr int kMaxBatch = 2048;  // sequences per launch (their prefix sums live in smem)
+constexpr int kTok = 16;           // tokens per pipeline stage
+constexpr int kMinLaunchBatch = 512;  // fewest sequences any configuration takes per launch
 
 enum : unsigned int { kSiteDecodeWait = 201, kSiteDecodeDrain = 202, kSiteBadBlock = 203 };
 
+// Warps per CTA: 12 for G = 2 and 4, where the consumer's arithmetic per byte
+// makes it latency-bound at two warps per scheduler and its registers still
+// allow three; else 8 (G = 1 streams at the HBM roofline with 8; G = 8 needs
+// 255 registers). With 12 the ring holds two stages per warp and a launch takes
+// up to 512 sequences (their prefix sums live in shared memory).
 template <int D, int G>
 struct DecCfg {
+  static constexpr int W = (G == 2 || G == 4) ? 12 : 8;
+  static constexpr int THREADS = W * 32;
+  static constexpr int MAXB = W == 12 ? kMinLaunchBatch : 2048;  // sequences per launch
   static constexpr int ROW = D * 2;                        // bytes of one token of one head
   static constexpr int KV = kTok * ROW;                    // K (or V) bytes of one stage
   static constexpr int QB = (G * D * 2 + 15) / 16 * 16;    // q bytes of one unit
   static constexpr int STAGE = 2 * KV + QB;
-  static constexpr int BUDGET = 196 * 1024 / kWarps;       // ring bytes per warp
-  static constexpr int STAGES = std::min(6, BUDGET / STAGE);
+  static constexpr int BUDGET = (W == 12 ? 210 : 196) * 1024 / W;  // ring bytes per warp
+  static constexpr int STAGES = std::max(2, std::min(6, BUDGET / STAGE));
   static constexpr int RING = STAGES * STAGE;
-  static constexpr int BAR_OFF = kWarps * RING;
-  static constexpr int META_OFF = BAR_OFF + kWarps * STAGES * 8;
-  static constexpr int PREFIX_OFF = META_OFF + kWarps * STAGES * 16;
-  static constexpr int CTX_OFF = PREFIX_OFF + (kMaxBatch + 1) * 4;
-  // G > 1: per warp two buffers of the stage's probabilities P [kTok][G] and
+  static constexpr int BAR_OFF = W * RING;
+  static constexpr int META_OFF = BAR_OFF + W * STAGES * 8;
+  static constexpr int PREFIX_OFF = META_OFF + W * STAGES * 16;
+  static constexpr int CTX_OFF = PREFIX_OFF + (MAXB + 1) * 4;
+  // G > 1: per warp a buffer of the stage's probabilities P [kTok][G] and
   // rescale factors alpha [G] (fp32), read back as broadcasts by every lane.
   static constexpr int PBUF = ((kTok + 1) * G * 4 + 15) / 16 * 16;
-  static constexpr int P_OFF = (CTX_OFF + kMaxBatch * 4 + 15) / 16 * 16;
-  static constexpr int SMEM = P_OFF + (G > 1 ? kWarps * 2 * PBUF : 0) + 16;
+  static constexpr int P_OFF = (CTX_OFF + MAXB * 4 + 15) / 16 * 16;
+  static constexpr int SMEM = P_OFF + (G > 1 ? W * PBUF : 0) + 16;
   static constexpr int E = D / 8;    // K elements per lane in the score phase
   static constexpr int DV = D / 32;  // output columns per lane
   static_assert(STAGES >= 2, "ring needs two stages");
@@ -130,7 +136,7 @@ __device__ __forceinline__ float scatter_sum8(const float (&v)[N], int l8) {
 }
 
 template <int D, int G>
-__global__ void __launch_bounds__(kThreads, 1) paged_decode_kernel(const DecParams p) {
+__global__ void __launch_bounds__(DecCfg<D, G>::THREADS, 1) paged_decode_kernel(const DecParams p) {
   using C = DecCfg<D, G>;
   extern __shared__ __align__(128) uint8_t smem[];
   const int warp = threadIdx.x >> 5;
@@ -146,8 +152,8 @@ __global__ void __launch_bounds__(kThreads, 1) paged_decode_kernel(const DecPara
 
   // Context lengths and the prefix sums of the splits per sequence: active
   // (sequence, split) pairs are numbered densely, v in [0, prefix[batch]).
-  for (int b = threadIdx.x; b < p.batch; b += kThreads) ctx_s[b] = max(p.ctx[b], 0);
-  if (threadIdx.x < kWarps * C::STAGES)
+  for (int b = threadIdx.x; b < p.batch; b += C::THREADS) ctx_s[b] = max(p.ctx[b], 0);
+  if (threadIdx.x < C::W * C::STAGES)
     mbar_init(reinterpret_cast<uint64_t*>(smem + C::BAR_OFF) + threadIdx.x, 1);
   if (threadIdx.x == 0) {
     *abort_flag = 0;
@@ -181,7 +187,7 @@ __global__ void __launch_bounds__(kThreads, 1) paged_decode_kernel(const DecPara
   __syncthreads();
   // Without a merge pass, rows of empty sequences are written here (zeros).
   if (p.direct_out && p.num_splits == 1 && blockIdx.x == 0) {
-    for (int b = warp; b < p.batch; b += kWarps) {
+    for (int b = warp; b < p.batch; b += C::W) {
       if (ctx_s[b] != 0) continue;
       for (int i = lane; i < p.hq * D / 2; i += 32)
         reinterpret_cast<uint32_t*>(p.out + static_cast<size_t>(b) * p.hq * D)[i] = 0u;
@@ -216,7 +222,7 @@ __global__ void __launch_bounds__(kThreads, 1) paged_decode_kernel(const DecPara
     pst = 0;
     pnst = (pend - pstart + kTok - 1) / kTok;
     bt_base = -(1 << 30);
-    if (lane == 0) nxt = kWarps * gridDim.x + atomicAdd(p.counter, 1u);
+    if (lane == 0) nxt = C::W * gridDim.x + atomicAdd(p.counter, 1u);
   };
 
   // Issue the copies of the producer's next stage into its ring slot.
@@ -280,7 +286,7 @@ __global__ void __launch_bounds__(kThreads, 1) paged_decode_kernel(const DecPara
   constexpr int HP = G > 1 ? G / 2 : 1;
   const int hown = l8 >> (3 - LG);
   const bool p_writer = (l8 & ((8 >> LG) - 1)) == 0;
-  float* pbuf = reinterpret_cast<float*>(smem + C::P_OFF) + warp * 2 * (C::PBUF / 4);
+  float* pbuf = reinterpret_cast<float*>(smem + C::P_OFF) + warp * (C::PBUF / 4);
   float m_own = -INFINITY, l_own = 0.f;
   uint64_t acc2[NACC][HP][C::DV];
 
@@ -342,9 +348,10 @@ __global__ void __launch_bounds__(kThreads, 1) paged_decode_kernel(const DecPara
     ps += __shfl_xor_sync(0xffffffffu, ps, 16);
     l_own = l_own * alpha + ps;
     m_own = mn;
-    // P [token][head] and alpha [head] to this stage's buffer (two alternate, so a
-    // lane that runs ahead never overwrites what another still reads).
-    float* pb = pbuf + (c_item & 1u) * (C::PBUF / 4);
+    // P [token][head] and alpha [head] to the warp's buffer. The __syncwarp after
+    // the last read of the previous stage keeps a lane that runs ahead from
+    // overwriting what another still reads.
+    float* pb = pbuf;
     if (p_writer) {
 #pragma unroll
       for (int step = 0; step < kTok / 4; ++step) pb[(step * 4 + grp) * G + hown] = s1[step];
@@ -792,7 +799,7 @@ struct DecodeWorkspace {
 DecodeWorkspace carve_workspace(void* base, int64_t batch, int64_t hq, int64_t d,
                                 int64_t num_splits) {
   DecodeWorkspace w;
-  const int64_t chunks = (batch + kMaxBatch - 1) / kMaxBatch;
+  const int64_t chunks = (batch + kMinLaunchBatch - 1) / kMinLaunchBatch;
   const size_t rows = static_cast<size_t>(batch) * hq;
   const size_t c_bytes = align256(static_cast<size_t>(chunks) * 4);
   const size_t o_bytes = align256(rows * num_splits * d * 4);
@@ -822,8 +829,26 @@ cudaError_t launch_decode_kernel(const DecParams& prm, int64_t upper_units, cons
   if (attr_err != cudaSuccess) return attr_err;
   // One CTA per SM, or one per unit when there are fewer units than SMs.
   const int grid = static_cast<int>(std::max<int64_t>(1, std::min<int64_t>(ctx.sm_count, upper_units)));
-  kern<<<grid, kThreads, C::SMEM, ctx.stream>>>(prm);
+  kern<<<grid, C::THREADS, C::SMEM, ctx.stream>>>(prm);
   return cudaGetLastError();
+}
+
+// Sequences one launch of the (d, g) configuration takes.
+int64_t launch_batch(int64_t d, int64_t g) {
+  if (d == 64) {
+    switch (g) {
+      case 1: return DecCfg<64, 1>::MAXB;
+      case 2: return DecCfg<64, 2>::MAXB;
+      case 4: return DecCfg<64, 4>::MAXB;
+      default: return DecCfg<64, 8>::MAXB;
+    }
+  }
+  switch (g) {
+    case 1: return DecCfg<128, 1>::MAXB;
+    case 2: return DecCfg<128, 2>::MAXB;
+    case 4: return DecCfg<128, 4>::MAXB;
+    default: return DecCfg<128, 8>::MAXB;
+  }
 }
 
 template <int D>
@@ -871,13 +896,14 @@ cudaError_t launch_paged_decode(const DecodeArgs& a, bool partials_mode, const L
     return cudaMemsetAsync(a.out, 0, static_cast<size_t>(rows) * a.d * 2, ctx.stream);
   }
   if (num_splits > 0) {
-    const int64_t chunks = (a.batch + kMaxBatch - 1) / kMaxBatch;
+    const int g = static_cast<int>(a.hq / a.hkv);
+    const int64_t per_launch = launch_batch(a.d, g);  // >= kMinLaunchBatch: one counter each
+    const int64_t chunks = (a.batch + per_launch - 1) / per_launch;
     cudaError_t e = cudaMemsetAsync(w.counters, 0, static_cast<size_t>(chunks) * 4, ctx.stream);
     if (e != cudaSuccess) return e;
-    const int g = static_cast<int>(a.hq / a.hkv);
     for (int64_t c = 0; c < chunks; ++c) {
-      const int64_t b0 = c * kMaxBatch;
-      const int64_t nb = std::min<int64_t>(kMaxBatch, a.batch - b0);
+      const int64_t b0 = c * per_launch;
+      const int64_t nb = std::min<int64_t>(per_launch, a.batch - b0);
       DecParams prm;
       prm.q = static_cast<const __half*>(a.q) + b0 * a.hq * a.d;
       prm.kc = static_cast<const __half*>(a.k_cache);
