@@ -19,7 +19,7 @@ Timing: W untimed warm-up steps, then exactly K steps between CUDA events on
 the launching stream, with a barrier and a device synchronize on both sides;
 the time is the max over ranks. Inputs are larger than L2 (126 MB) in every
 timed case, so no flush is needed between steps. SM clocks and clock-event
-reasons are read through NVML every 2 ms during the warm-up and timed steps
+reasons are read through NVML every 1 ms during the warm-up and timed steps
 (`clocks` in the line). Data are synthetic (seeded N(0, 1) fp16), no dataset is
 involved.
 
@@ -209,7 +209,7 @@ class NvmlClockSampler:
     BITS = {"sw_power_cap": 0x4, "hw_slowdown": 0x8, "sw_thermal_slowdown": 0x20,
             "hw_thermal_slowdown": 0x40}
 
-    def __init__(self, device: torch.device, period_s=0.002):
+    def __init__(self, device: torch.device, period_s=0.001):
         self.device, self.period = device, period_s
         self.fallback = None
         self.sm, self.mx, self.reasons = [], [], set()
@@ -227,19 +227,26 @@ class NvmlClockSampler:
             self.fallback = ClockSampler(self.device.index or 0).__enter__()
             return self
         self.stop = threading.Event()
+        try:
+            self.mx.append(self.nvml.nvmlDeviceGetMaxClockInfo(self.handle, self.nvml.NVML_CLOCK_SM))
+        except Exception:  # noqa: BLE001
+            pass
 
         def run():
             nv, h = self.nvml, self.handle
             while not self.stop.is_set():
                 try:
                     self.sm.append(nv.nvmlDeviceGetClockInfo(h, nv.NVML_CLOCK_SM))
-                    self.mx.append(nv.nvmlDeviceGetMaxClockInfo(h, nv.NVML_CLOCK_SM))
                     bits = nv.nvmlDeviceGetCurrentClocksEventReasons(h)
                     self.reasons.update(n for n, b in self.BITS.items() if bits & b)
                 except Exception:  # noqa: BLE001
                     break
                 self.stop.wait(self.period)
 
+        # A short interpreter switch interval lets the sampling thread take the GIL
+        # between the main thread's launches, not only while it waits on the device.
+        self.switch = sys.getswitchinterval()
+        sys.setswitchinterval(2e-4)
         self.thread = threading.Thread(target=run, daemon=True)
         self.thread.start()
         return self
@@ -249,6 +256,7 @@ class NvmlClockSampler:
             return self.fallback.__exit__(*exc)
         self.stop.set()
         self.thread.join(timeout=5)
+        sys.setswitchinterval(self.switch)
         try:
             self.nvml.nvmlShutdown()
         except Exception:  # noqa: BLE001
@@ -260,7 +268,8 @@ class NvmlClockSampler:
             return self.fallback.summary()
         if not self.sm:
             return {"sm_mhz": None, "sm_max_mhz": None, "reasons": [], "samples": 0}
-        return {"sm_mhz": statistics.median(self.sm), "sm_max_mhz": max(self.mx),
+        return {"sm_mhz": statistics.median(self.sm),
+                "sm_max_mhz": max(self.mx) if self.mx else None,
                 "reasons": sorted(self.reasons), "samples": len(self.sm),
                 "source": f"NVML every {self.period * 1e3:.0f} ms during warm-up and timed steps"}
 
@@ -707,6 +716,15 @@ def profile_case(kind, d: Dist):
         shape = (c["batch"], c["heads"], c["seq"], c["head_dim"])
         q, k, v = (randn_half(shape, gen, d.device) for _ in range(3))
         fn = lambda: ak.flash_attention(q, k, v, causal=True)  # noqa: E731
+    elif kind == "decode_gqa":
+        # The reference's results-table decode layer (32 query over 8 kv heads, d 128,
+        # block 16) at 64 sequences of 8192 tokens: 2.1 GB of K/V, partition 512.
+        ctx = [8192] * 64
+        kc, vc, tables, lens = synthetic_paged_cache(ctx, 8, 128, 16, 4200, d.device)
+        q = randn_half((64, 32, 128), torch.Generator(device=d.device).manual_seed(2),
+                       d.device)
+        fn = lambda: ak.paged_decode(q, kc, vc, tables, lens, 8192,  # noqa: E731
+                                     partition_size=512)
     else:
         c = CFG4  # batch 16 of config 4: about 1.1 GB of K/V
         g = torch.Generator().manual_seed(4000)
@@ -777,7 +795,7 @@ def main():
                          "clocks are sampled during the timed steps themselves)")
     ap.add_argument("--ablation", action="store_true",
                     help="print the decode split-size ablation (one JSON list) and exit")
-    ap.add_argument("--profile", choices=["prefill", "decode"],
+    ap.add_argument("--profile", choices=["prefill", "decode", "decode_gqa"],
                     help="run one small case of a kernel (3 + 2 launches) for ncu, no timing")
     args = ap.parse_args()
     if args.warmup < 3:

@@ -96,41 +96,31 @@ struct DecParams {
 
 
 // Sums N partial values over the 8 lanes of a token group (lane bits 4, 2, 1 of
-// l8) and scatters them: the lane returns the full sum of value l8 >> (3 - log2 N).
-// N - 1 shuffles instead of 3 N for N separate butterflies.
+// l8) and scatters them, in N - 1 shuffles instead of 3 N for N separate
+// butterflies. The lane's values come permuted: v[i] is value i ^ own, own =
+// l8 >> (3 - log2 N), so at every level a lane keeps the first half and sends the
+// second, which its partner (own differing in that level's bit) holds as its own
+// first half. Returns the full sum of value `own`.
 template <int N>
-__device__ __forceinline__ float scatter_sum8(const float (&v)[N], int l8) {
+__device__ __forceinline__ float scatter_sum8(const float (&v)[N]) {
   static_assert(N == 2 || N == 4 || N == 8, "two to eight values");
   constexpr int H1 = N / 2;
-  const bool b2 = (l8 & 4) != 0;
   float w[H1];
 #pragma unroll
-  for (int i = 0; i < H1; ++i) {  // w[i]: value (b2 ? H1 : 0) + i over lanes {l, l ^ 4}
-    const float send = b2 ? v[i] : v[H1 + i];
-    const float keep = b2 ? v[H1 + i] : v[i];
-    w[i] = keep + __shfl_xor_sync(0xffffffffu, send, 4);
-  }
+  for (int i = 0; i < H1; ++i) w[i] = v[i] + __shfl_xor_sync(0xffffffffu, v[H1 + i], 4);
   if constexpr (N == 2) {
     float x = w[0];
     x += __shfl_xor_sync(0xffffffffu, x, 2);
     return x + __shfl_xor_sync(0xffffffffu, x, 1);
   } else {
     constexpr int H2 = N / 4;
-    const bool b1 = (l8 & 2) != 0;
     float u[H2];
 #pragma unroll
-    for (int i = 0; i < H2; ++i) {
-      const float send = b1 ? w[i] : w[H2 + i];
-      const float keep = b1 ? w[H2 + i] : w[i];
-      u[i] = keep + __shfl_xor_sync(0xffffffffu, send, 2);
-    }
+    for (int i = 0; i < H2; ++i) u[i] = w[i] + __shfl_xor_sync(0xffffffffu, w[H2 + i], 2);
     if constexpr (N == 4) {
       return u[0] + __shfl_xor_sync(0xffffffffu, u[0], 1);
     } else {
-      const bool b0 = (l8 & 1) != 0;
-      const float send = b0 ? u[0] : u[1];
-      const float keep = b0 ? u[1] : u[0];
-      return keep + __shfl_xor_sync(0xffffffffu, send, 1);
+      return u[0] + __shfl_xor_sync(0xffffffffu, u[1], 1);
     }
   }
 }
@@ -271,7 +261,8 @@ __global__ void __launch_bounds__(DecCfg<D, G>::THREADS, 1) paged_decode_kernel(
 
   // ---------------------------------------------------------- consumer state
   // q * scale * log2(e) as packed fp32 pairs: the 16 (or 8) elements this lane
-  // multiplies in the score phase.
+  // multiplies in the score phase; slot g holds head g ^ hown (the order
+  // scatter_sum8 takes; hown = 0 for G = 1).
   uint64_t qf[G][C::E / 2];
   float m[G], l[G];
   // Output columns [lane * DV, lane * DV + DV) as DV / 2 packed pairs. With
@@ -329,7 +320,7 @@ __global__ void __launch_bounds__(DecCfg<D, G>::THREADS, 1) paged_decode_kernel(
         f2_unpack(f2_add(d0, d1), a, b);
         dot[g] = a + b;
       }
-      const float v = scatter_sum8<G>(dot, l8);
+      const float v = scatter_sum8<G>(dot);
       s1[step] = (t < nt) ? v : -INFINITY;
     }
     // Online softmax of this lane's head over the stage's 16 tokens (4 token groups).
@@ -465,7 +456,7 @@ __global__ void __launch_bounds__(DecCfg<D, G>::THREADS, 1) paged_decode_kernel(
       for (int g = 0; g < G; ++g) {
 #pragma unroll
         for (int e8 = 0; e8 < C::E / 8; ++e8) {
-          const uint4 raw = *reinterpret_cast<const uint4*>(qs + g * D + e8 * 64 + l8 * 8);
+          const uint4 raw = *reinterpret_cast<const uint4*>(qs + (g ^ hown) * D + e8 * 64 + l8 * 8);
           qf[g][e8 * 4 + 0] = f2_mul(half2_pair(raw.x), sc);
           qf[g][e8 * 4 + 1] = f2_mul(half2_pair(raw.y), sc);
           qf[g][e8 * 4 + 2] = f2_mul(half2_pair(raw.z), sc);
