@@ -874,13 +874,44 @@ cudaError_t launch_merge_impl(const MergeParams& mp, int d, cudaStream_t stream)
 
 }  // namespace
 
+// Sub-splits. A call with few (sequence, kv head, split) units leaves most of the
+// resident warps idle while each busy warp walks its split one 16-token stage at
+// a time, so the launch takes about (tokens per split / 16) stage latencies. Such
+// calls cut every partition into k = 2 or 4 sub-partitions (at least 64 tokens)
+// that are merged like splits; the result differs from k = 1 only by rounding.
+// The workspace is sized for the largest k the sizes allow (a bound on the
+// partial rows that keeps it small), so sizing needs no device query; the launch
+// picks k from the units and the resident warps of the device.
+constexpr int64_t kSubRowBudget = 8192;  // (sequence, query head, part) rows at most
+
+int64_t sub_split_cap(int64_t batch, int64_t hq, int64_t max_ctx, int64_t partition) {
+  const int64_t rows = batch * hq * splits_of(max_ctx, partition);
+  for (int64_t k = 4; k > 1; k /= 2)
+    if (partition / k >= 64 && rows * k <= kSubRowBudget) return k;
+  return 1;
+}
+
+int64_t resident_warps(int64_t d, int64_t g, int64_t sm_count) {
+  const int64_t w = d == 64 ? (g == 1 ? DecCfg<64, 1>::W : g == 2 ? DecCfg<64, 2>::W
+                                       : g == 4 ? DecCfg<64, 4>::W : DecCfg<64, 8>::W)
+                            : (g == 1 ? DecCfg<128, 1>::W : g == 2 ? DecCfg<128, 2>::W
+                                       : g == 4 ? DecCfg<128, 4>::W : DecCfg<128, 8>::W);
+  return w * sm_count;
+}
+
 size_t decode_workspace_bytes(int64_t batch, int64_t hq, int64_t d, int64_t max_ctx,
                               int64_t partition) {
-  return carve_workspace(nullptr, batch, hq, d, splits_of(max_ctx, partition)).bytes;
+  const int64_t cap = sub_split_cap(batch, hq, max_ctx, partition);
+  return carve_workspace(nullptr, batch, hq, d, splits_of(max_ctx, partition) * cap).bytes;
 }
 
 cudaError_t launch_paged_decode(const DecodeArgs& a, bool partials_mode, const LaunchCtx& ctx) {
-  const int64_t num_splits = splits_of(a.max_ctx, a.partition);
+  // Sub-split only while the units stay within one per resident warp.
+  int64_t k = sub_split_cap(a.batch, a.hq, a.max_ctx, a.partition);
+  const int64_t units = a.batch * a.hkv * splits_of(a.max_ctx, a.partition);
+  while (k > 1 && units * k > resident_warps(a.d, a.hq / a.hkv, ctx.sm_count)) k /= 2;
+  const int64_t part = a.partition / k;
+  const int64_t num_splits = splits_of(a.max_ctx, part);
   const int64_t rows = a.batch * a.hq;
   DecodeWorkspace w = carve_workspace(a.workspace, a.batch, a.hq, a.d, num_splits);
   if (num_splits == 0 && !partials_mode) {
@@ -914,7 +945,7 @@ cudaError_t launch_paged_decode(const DecodeArgs& a, bool partials_mode, const L
       prm.hkv = static_cast<int>(a.hkv);
       prm.bs = static_cast<int>(a.bs);
       prm.max_blocks = static_cast<int>(a.max_blocks);
-      prm.partition = static_cast<int>(a.partition);
+      prm.partition = static_cast<int>(part);
       prm.num_blocks = static_cast<int>(a.num_blocks);
       prm.num_splits = static_cast<int>(num_splits);
       prm.direct_out = partials_mode ? 0 : 1;
@@ -937,7 +968,7 @@ cudaError_t launch_paged_decode(const DecodeArgs& a, bool partials_mode, const L
   mp.ml_row_stride = num_splits;
   mp.ml_part_stride = 1;
   mp.hq = static_cast<int>(a.hq);
-  mp.partition = static_cast<int>(a.partition);
+  mp.partition = static_cast<int>(part);
   mp.num_parts = static_cast<int>(num_splits);
   mp.skip_single = partials_mode ? 0 : 1;
   mp.out16 = partials_mode ? nullptr : static_cast<__half*>(a.out);

@@ -95,8 +95,12 @@ int attn_naive_fwd(const void* q, const void* k, const void* v, void* o, int64_t
 
 /*
  * Bytes of workspace attn_paged_decode / attn_paged_decode_partials need for
- * split-K partials (fp32 o, m, l per (sequence, query head, split)) and the
- * work counter. num_splits = ceil(max_context_len / partition).
+ * split-K partials (fp32 o, m, l per (sequence, query head, part)) and the
+ * work counters: parts = k * ceil(max_context_len / partition), where k = 4 or 2
+ * while batch * num_heads * parts stays within 8192 rows (and partition / k >= 64
+ * tokens), else 1. Calls with that few partial rows may cut each partition into
+ * k sub-partitions so that more warps share a short decode; the output differs
+ * only by rounding.
  */
 size_t attn_paged_decode_workspace_bytes(int64_t batch, int64_t num_heads, int64_t head_dim,
                                          int64_t max_context_len, int64_t partition);

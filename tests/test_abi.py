@@ -88,12 +88,14 @@ def test_decode_rejects_like_the_reference(lib):
 
 
 def test_decode_workspace_size(lib):
-    # counters (256) + o [B*H*S*D] fp32 + m, l [B*H*S] fp32, each 256-byte aligned.
-    b, h, d, ctx, part = 3, 4, 128, 1000, 256
-    s = -(-ctx // part)
+    # counters (256 per 512 sequences) + o [B*H*S*D] fp32 + m, l [B*H*S] fp32, each
+    # 256-byte aligned; S = k * ceil(ctx / part), k = 4 or 2 while B*H*S <= 8192 rows.
     align = lambda x: -(-x // 256) * 256  # noqa: E731
-    want = 256 + align(b * h * s * d * 4) + 2 * align(b * h * s * 4)
-    assert lib.attn_paged_decode_workspace_bytes(b, h, d, ctx, part) == want
+    for b, h, d, ctx, part, k in [(3, 4, 128, 1000, 256, 4), (64, 32, 128, 8192, 512, 1),
+                                  (1, 32, 64, 32768, 256, 2), (1, 32, 128, 32768, 1024, 4)]:
+        s = -(-ctx // part) * k
+        want = align(-(-b // 512) * 4) + align(b * h * s * d * 4) + 2 * align(b * h * s * 4)
+        assert lib.attn_paged_decode_workspace_bytes(b, h, d, ctx, part) == want, (b, h, ctx)
     assert lib.attn_naive_workspace_bytes(2, 3, 100) == 2 * 3 * 100 * 100 * 4
 
 
