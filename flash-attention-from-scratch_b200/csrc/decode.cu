@@ -264,7 +264,7 @@ __global__ void __launch_bounds__(DecCfg<D, G>::THREADS, 1) paged_decode_kernel(
   // multiplies in the score phase; slot g holds head g ^ hown (the order
   // scatter_sum8 takes; hown = 0 for G = 1).
   uint64_t qf[G][C::E / 2];
-  float m[G], l[G];
+  float m[G], l[G];  // G = 1 only (G > 1 keeps m_own, l_own below)
   // Output columns [lane * DV, lane * DV + DV) as DV / 2 packed pairs. With
   // G <= 2 two accumulator sets (even / odd tokens) halve the FMA chains.
   constexpr int NACC = G <= 2 ? 2 : 1;
@@ -462,21 +462,25 @@ __global__ void __launch_bounds__(DecCfg<D, G>::THREADS, 1) paged_decode_kernel(
           qf[g][e8 * 4 + 2] = f2_mul(half2_pair(raw.z), sc);
           qf[g][e8 * 4 + 3] = f2_mul(half2_pair(raw.w), sc);
         }
-        m[g] = -INFINITY;
-        l[g] = 0.f;
+        if constexpr (G == 1) {
+          m[g] = -INFINITY;
+          l[g] = 0.f;
+#pragma unroll
+          for (int a = 0; a < NACC; ++a)
+#pragma unroll
+            for (int j = 0; j < C::DV / 2; ++j) acc[a][g][j] = f2_pack(0.f, 0.f);
+        }
+      }
+      if constexpr (G > 1) {
+        m_own = -INFINITY;
+        l_own = 0.f;
 #pragma unroll
         for (int a = 0; a < NACC; ++a)
 #pragma unroll
-          for (int j = 0; j < C::DV / 2; ++j) acc[a][g][j] = f2_pack(0.f, 0.f);
+          for (int i = 0; i < HP; ++i)
+#pragma unroll
+            for (int j = 0; j < C::DV; ++j) acc2[a][i][j] = f2_pack(0.f, 0.f);
       }
-      m_own = -INFINITY;
-      l_own = 0.f;
-#pragma unroll
-      for (int a = 0; a < NACC; ++a)
-#pragma unroll
-        for (int i = 0; i < HP; ++i)
-#pragma unroll
-          for (int j = 0; j < C::DV; ++j) acc2[a][i][j] = f2_pack(0.f, 0.f);
     }
     if constexpr (G > 1) {
       consume_grouped(st, nt, md);
