@@ -16,7 +16,8 @@ Decode (one query token per sequence) over a paged KV cache:
 
 Additions (no counterpart in the reference): paged_decode_partials and
 merge_partials expose the split state for context parallelism across GPUs
-(see attnkernels.parallel), and device_status reads the kernels' error word.
+(see attnkernels.parallel), device_status reads the kernels' error word, and
+release_workspaces drops the decode scratch kept between calls.
 
 There is no CPU fallback: every function needs a B200 and the native library
 (built by flash-attention-from-scratch_b200/build.py, or on first use).
@@ -32,7 +33,7 @@ from . import _native
 
 __all__ = ["naive_attention", "flash_attention", "paged_decode", "decode_partition",
            "load_extension", "paged_decode_partials", "merge_partials", "device_status",
-           "check_device_status", "CHUNK", "WMMA_BLOCK_N"]
+           "check_device_status", "release_workspaces", "CHUNK", "WMMA_BLOCK_N"]
 
 # Decode partitions are multiples of this many tokens (attnkernels/__init__.py:29).
 CHUNK = 256
@@ -239,6 +240,13 @@ def merge_partials(o_parts, m_parts, l_parts, out=None):
         raise ValueError("m_parts and l_parts must share their part stride")
     return load_extension().merge_partials(o_parts, m_parts, l_parts, rows, D, o_stride,
                                            ml_stride, P, out)
+
+
+def release_workspaces():
+    """Drop the decode scratch buffers kept per (device, stream) between calls (the
+    split-K partials), so the caching allocator can reuse or free their memory.
+    Call it when no decode is in flight on those streams."""
+    _native._decode_ws.clear()
 
 
 def device_status(device=None):

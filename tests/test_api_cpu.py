@@ -86,3 +86,9 @@ def test_context_range_is_block_aligned():
 def test_head_and_pair_ranges():
     assert parallel.head_range(32, 8, 7) == (28, 32)
     assert parallel.pair_range(4, 16, 8, 1) == (8, 16)
+
+
+def test_release_workspaces_empties_the_cache():
+    from attnkernels import _native
+    ak.release_workspaces()
+    assert _native._decode_ws._bufs == {}
