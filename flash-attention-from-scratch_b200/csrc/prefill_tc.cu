@@ -185,7 +185,13 @@ __global__ void __launch_bounds__(TcCfg<D, NQ>::THREADS, 1)
   }
   const int nkv_max = kv_tiles_of(p, min(qt0 + NQ - 1, p.n_tiles - 1));
 
-  if (threadIdx.x == 0) {
+  // The TMA producer thread initialises the barriers and issues Q and the first
+  // ring loads before the CTA-wide barrier, so those copies overlap the tensor
+  // memory allocation and the barrier itself. A ring slot's first use needs no
+  // wait; `issued` carries the count into the producer loop.
+  const bool producer = warp == C::LOAD_WARP && lane == 0;
+  int issued = 0;
+  if (producer) {
     mbar_init(q_full, 1);
     for (int s = 0; s < C::SLOTS; ++s) {
       mbar_init(full + s, 1);
@@ -201,15 +207,29 @@ __global__ void __launch_bounds__(TcCfg<D, NQ>::THREADS, 1)
     for (int s = 0; s < C::PAIRS; ++s) mbar_init(step_full + s, 1);
     *abort_flag = 0;
     fence_mbar_init();
+    prefetch_tensormap(&p.tq);
+    prefetch_tensormap(&p.tk);
+    prefetch_tensormap(&p.tv);
+    int nq = 0;
+    for (int i = 0; i < NQ; ++i) nq += (qt0 + i < p.n_tiles) ? 1 : 0;
+    mbar_arrive_expect_tx(q_full, nq * C::TILE_BYTES);
+    for (int i = 0; i < nq; ++i)
+      for (int h = 0; h < C::NHALF; ++h)
+        tma_load_3d(smem + C::Q_OFF + i * C::TILE_BYTES + h * C::BLK_BYTES, &p.tq, q_full,
+                    h * 64, (qt0 + i) * kBM, bh);
+    // Item 2 j is K_j and item 2 j + 1 is V_j; item `it` goes to slot
+    // it % SLOTS on its (it / SLOTS)-th use of that slot.
+    for (; issued < 2 * nkv_max && issued < C::SLOTS; ++issued) {
+      mbar_arrive_expect_tx(full + issued, C::TILE_BYTES);
+      const CUtensorMap* map = (issued & 1) ? &p.tv : &p.tk;
+      for (int h = 0; h < C::NHALF; ++h)
+        tma_load_3d(smem + C::RING_OFF + issued * C::TILE_BYTES + h * C::BLK_BYTES, map,
+                    full + issued, h * 64, (issued >> 1) * kBN, bh);
+    }
   }
   if (warp == C::MMA_WARP) {
     tmem_alloc(tmem_slot, C::TMEM_COLS);
     tmem_relinquish();
-  }
-  if (warp == C::LOAD_WARP && lane == 0) {
-    prefetch_tensormap(&p.tq);
-    prefetch_tensormap(&p.tk);
-    prefetch_tensormap(&p.tv);
   }
   tc_fence_before();
   __syncthreads();
@@ -222,18 +242,9 @@ __global__ void __launch_bounds__(TcCfg<D, NQ>::THREADS, 1)
     asm volatile("setmaxnreg.dec.sync.aligned.u32 %0;" ::"n"(C::CONTROL_REGS));
     if (warp == C::LOAD_WARP) {
     // ------------------------------------------------------------ TMA producer
-    if (lane == 0) {
-      int nq = 0;
-      for (int i = 0; i < NQ; ++i) nq += (qt0 + i < p.n_tiles) ? 1 : 0;
-      mbar_arrive_expect_tx(q_full, nq * C::TILE_BYTES);
-      for (int i = 0; i < nq; ++i)
-        for (int h = 0; h < C::NHALF; ++h)
-          tma_load_3d(smem + C::Q_OFF + i * C::TILE_BYTES + h * C::BLK_BYTES, &p.tq, q_full,
-                      h * 64, (qt0 + i) * kBM, bh);
-      // Item 2 j is K_j and item 2 j + 1 is V_j; item `it` goes to slot
-      // it % SLOTS on its (it / SLOTS)-th use of that slot.
-      int issued = 0;
-      for (int it = 0; it < 2 * nkv_max; ++it) {
+    if (producer) {
+      // Q and the first SLOTS ring items were issued before the CTA barrier.
+      for (int it = issued; it < 2 * nkv_max; ++it) {
         const int slot = it % C::SLOTS;
         if (!mbar_wait(empty + slot, ((it / C::SLOTS) & 1) ^ 1, abort_flag, p.status,
                        (it & 1) ? kSiteLoadV : kSiteLoadK, p.timeout_ns))
