@@ -441,6 +441,39 @@ def bench_prefill_cfg2(args, d: Dist, peaks, peak_src, traffic):
     return res
 
 
+def bench_prefill_shapes(args, d: Dist, peaks, peak_src, traffic):
+    """The other two shapes BASELINE config 2 names: d=64 and N=4095 (odd length,
+    tail masking), same batch and heads, causal; one batch per rank, device-timed
+    like the headline, each with its own clock record."""
+    import attnkernels as ak
+
+    out = {}
+    for key, d_head, n in (("d64", 64, 4096), ("n4095", 128, 4095)):
+        c = dict(CFG2, head_dim=d_head, seq=n)
+        shape = (c["batch"], c["heads"], c["seq"], c["head_dim"])
+        gen = torch.Generator(device=d.device).manual_seed(1100 + d.rank)
+        q, k, v = (randn_half(shape, gen, d.device) for _ in range(3))
+        fn = lambda: ak.flash_attention(q, k, v, causal=True)  # noqa: E731
+        with NvmlClockSampler(d.device) as clk:
+            ms = timed(fn, args.steps, args.warmup, d)
+        flops = prefill_flops(**c)
+        out[key] = {
+            "workload": f"causal prefill B={c['batch']} H={c['heads']} N={n} d={d_head} "
+                        "(BASELINE config 2 variant), one batch per GPU",
+            "ms_per_step": round(ms / args.steps, 4),
+            "value": round(flops * d.world / (ms / args.steps * 1e-3) / 1e12, 2),
+            "unit": "TFLOP/s",
+            "roofline": roofline("tensor", flops, ms / args.steps, peaks, peak_src,
+                                 traffic.get(f"flash_tc_kernel_cfg2_{key}")),
+            "clocks": clk.summary(),
+            "gpu_launches": args.steps,
+            "l2": "inputs larger than L2 (q, k, v %d MiB per step), no flush"
+                  % (3 * q.numel() * 2 >> 20)}
+        del q, k, v
+    torch.cuda.empty_cache()
+    return out
+
+
 def bench_decode_cfg4(args, d: Dist, peaks, peak_src, traffic):
     """Config 4 per rank (independent sequences: weak scaling)."""
     import attnkernels as ak
@@ -574,8 +607,11 @@ def torch_comparison(args, d: Dist, ours_prefill, ours_decode):
     return out
 
 
-def bench_long_context(args, d: Dist, peaks, peak_src):
-    """Configs 3 and 5, total work fixed and split over the ranks (strong scaling)."""
+def bench_long_context(args, d: Dist, peaks, peak_src, traffic):
+    """Configs 3 and 5, total work fixed and split over the ranks (strong scaling).
+    Each entry carries its own NVML clock record; `traffic` is the per-launch DRAM
+    bytes of one rank's kernel, from a smaller ncu capture scaled by the units
+    processed (profiles/traffic.json)."""
     import attnkernels as ak
     from attnkernels import parallel
 
@@ -586,14 +622,18 @@ def bench_long_context(args, d: Dist, peaks, peak_src):
     gen = torch.Generator(device=d.device).manual_seed(3000 + h0)
     shape = (c["batch"], h1 - h0, c["seq"], c["head_dim"])
     q, k, v = (randn_half(shape, gen, d.device, c["input_scale"]) for _ in range(3))
-    ms = timed(lambda: ak.flash_attention(q, k, v, causal=True), args.steps, args.warmup, d)
+    with NvmlClockSampler(d.device) as clk:
+        ms = timed(lambda: ak.flash_attention(q, k, v, causal=True), args.steps, args.warmup, d)
     flops = prefill_flops(**{x: c[x] for x in ("batch", "heads", "seq", "head_dim", "causal")})
     per_rank = prefill_flops(c["batch"], h1 - h0, c["seq"], c["head_dim"], True)
+    t3 = traffic.get("flash_tc_kernel_cfg3_per_head")
     out["config3_prefill"] = {
         "workload": "causal prefill B=1 H=32 N=32768 d=128, heads sharded over ranks",
         "heads_per_rank": h1 - h0, "scaling": "strong", "ms_per_step": round(ms / args.steps, 4),
         "value": round(flops / (ms / args.steps * 1e-3) / 1e12, 2), "unit": "TFLOP/s",
-        "roofline": roofline("tensor", per_rank, ms / args.steps, peaks, peak_src),
+        "roofline": roofline("tensor", per_rank, ms / args.steps, peaks, peak_src,
+                             None if t3 is None else int(t3 * (h1 - h0))),
+        "clocks": clk.summary(),
         "gpu_launches": args.steps}
     del q, k, v
     torch.cuda.empty_cache()
@@ -613,19 +653,30 @@ def bench_long_context(args, d: Dist, peaks, peak_src):
                                      partition_size=part)
         launches = 2
     else:
-        cp = parallel.ContextParallelDecode()
+        cp = parallel.ContextParallelDecode(chunks=args.cp_chunks)
         fn = lambda: cp(q, kc, vc, tables, lens, t1 - t0, partition_size=part)  # noqa: E731
-        launches = 3
-    ms = timed(fn, args.steps, args.warmup, d)
+        # per chunk: decode kernel + local split-K merge + the merge across ranks
+        launches = 3 * min(args.cp_chunks, c["batch"])
+    with NvmlClockSampler(d.device) as clk:
+        ms = timed(fn, args.steps, args.warmup, d)
     total = kv_bytes([c["ctx"]] * c["batch"], c["kv_heads"], c["head_dim"])
+    t5 = traffic.get("paged_decode_kernel_cfg5_per_token")
     out["config5_decode"] = {
         "workload": "paged decode B=8 H=32 d=128 ctx=131072, context ranges over ranks, "
                     "NCCL all-gather + merge of the (o, m, l) partials",
         "tokens_per_rank": t1 - t0, "partition": part, "scaling": "strong",
         "ms_per_step": round(ms / args.steps, 4),
         "value": round(total / (ms / args.steps * 1e-3) / 1e9, 1), "unit": "GB/s",
-        "roofline": roofline("hbm", total / d.world, ms / args.steps, peaks, peak_src),
+        "roofline": roofline("hbm", total / d.world, ms / args.steps, peaks, peak_src,
+                             None if t5 is None else int(t5 * (t1 - t0) * c["batch"])),
+        "clocks": clk.summary(),
         "gpu_launches": launches * args.steps}
+    if d.world > 1:
+        out["config5_decode"]["exchange"] = (
+            f"NCCL all_gather_into_tensor of {c['batch'] * c['heads'] * (c['head_dim'] + 2) * 4} "
+            f"bytes per rank, then the merge kernel; batch cut into "
+            f"{min(args.cp_chunks, c['batch'])} chunk(s) whose exchanges overlap the next "
+            f"chunk's decode")
     return out
 
 
@@ -716,6 +767,31 @@ def profile_case(kind, d: Dist):
         shape = (c["batch"], c["heads"], c["seq"], c["head_dim"])
         q, k, v = (randn_half(shape, gen, d.device) for _ in range(3))
         fn = lambda: ak.flash_attention(q, k, v, causal=True)  # noqa: E731
+    elif kind in ("prefill_d64", "prefill_n4095"):
+        c = dict(CFG2, head_dim=64) if kind == "prefill_d64" else dict(CFG2, seq=4095)
+        gen = torch.Generator(device=d.device).manual_seed(1100)
+        shape = (c["batch"], c["heads"], c["seq"], c["head_dim"])
+        q, k, v = (randn_half(shape, gen, d.device) for _ in range(3))
+        fn = lambda: ak.flash_attention(q, k, v, causal=True)  # noqa: E731
+    elif kind == "prefill_long":
+        # 8 of config 3's 32 heads (q, k, v 192 MiB, above L2): its DRAM bytes per head
+        # scale to a rank's share of config 3.
+        c = CFG3
+        gen = torch.Generator(device=d.device).manual_seed(3000)
+        shape = (1, 8, c["seq"], c["head_dim"])
+        q, k, v = (randn_half(shape, gen, d.device, c["input_scale"]) for _ in range(3))
+        fn = lambda: ak.flash_attention(q, k, v, causal=True)  # noqa: E731
+    elif kind == "decode_long":
+        # One sequence of config 5's 131072 tokens, 32 heads (2.1 GB of K/V); DRAM bytes
+        # per token scale to a rank's share of config 5.
+        c = CFG5
+        kc, vc, tables, lens = synthetic_paged_cache([c["ctx"]], c["kv_heads"], c["head_dim"],
+                                                     c["block_size"], 5000, d.device)
+        q = randn_half((1, c["heads"], c["head_dim"]),
+                       torch.Generator(device=d.device).manual_seed(5100), d.device)
+        part = ak.decode_partition(1, c["kv_heads"], c["ctx"])
+        fn = lambda: ak.paged_decode(q, kc, vc, tables, lens, c["ctx"],  # noqa: E731
+                                     partition_size=part)
     elif kind == "decode_gqa":
         # The reference's results-table decode layer (32 query over 8 kv heads, d 128,
         # block 16) at 64 sequences of 8192 tokens: 2.1 GB of K/V, partition 512.
@@ -793,9 +869,14 @@ def main():
     ap.add_argument("--spin", type=float, default=0.0,
                     help="seconds of untimed load before a timed region (default none: the "
                          "clocks are sampled during the timed steps themselves)")
+    ap.add_argument("--cp-chunks", type=int, default=1,
+                    help="batch chunks of the context-parallel decode at N > 1 (each "
+                         "chunk's exchange overlaps the next chunk's decode)")
     ap.add_argument("--ablation", action="store_true",
                     help="print the decode split-size ablation (one JSON list) and exit")
-    ap.add_argument("--profile", choices=["prefill", "decode", "decode_gqa"],
+    ap.add_argument("--profile", choices=["prefill", "prefill_d64", "prefill_n4095",
+                                          "prefill_long", "decode", "decode_gqa",
+                                          "decode_long"],
                     help="run one small case of a kernel (3 + 2 launches) for ncu, no timing")
     args = ap.parse_args()
     if args.warmup < 3:
@@ -822,6 +903,8 @@ def main():
     peaks, peak_src = load_peaks()
     traffic = load_traffic()
     pre = bench_prefill_cfg2(args, d, peaks, peak_src, traffic)
+    shapes = None if args.only_prefill else bench_prefill_shapes(args, d, peaks, peak_src,
+                                                                 traffic)
     line = {
         "metric": BASELINE_METRIC,
         "value": round(pre["value"], 2),
@@ -846,10 +929,12 @@ def main():
         "per_rank_ms_per_step": pre["per_rank_ms_per_step"],
         "clocks": pre["clocks"],
     }
+    if shapes is not None:
+        line["prefill_cfg2_shapes"] = shapes
     if not args.only_prefill:
         line["decode"] = bench_decode_cfg4(args, d, peaks, peak_src, traffic)
         if not args.no_long:
-            line["long_context"] = bench_long_context(args, d, peaks, peak_src)
+            line["long_context"] = bench_long_context(args, d, peaks, peak_src, traffic)
         if d.world == 1 and not args.no_compare:
             line["torch_comparison"] = torch_comparison(args, d, line["value"],
                                                         line["decode"]["value"])

@@ -49,6 +49,7 @@ SIGNATURES = {
                                          _i64, _i64, _i64, _i64, _f32, _i64, _vp]),
     "attn_device_status": (_int, [_u32p, _u32p]),
     "attn_selftest_wait_timeout": (_int, [ctypes.c_uint64, _vp]),
+    "attn_selftest_exp2": (_int, [_vp, _vp, _vp, _vp, _i64, _vp]),
 }
 
 ABI_VERSION = 1
@@ -236,6 +237,18 @@ class Extension:
         with torch.cuda.device(dev):
             _check(self.lib.attn_device_status(ctypes.byref(code), ctypes.byref(site)))
         return code.value, site.value
+
+    def selftest_exp2(self, x):
+        """(poly, mufu, exp2f) of fp32 CUDA tensor x: the prefill softmax's two
+        exponentials and CUDA's exp2f, elementwise."""
+        x = x.contiguous()
+        if x.dtype != torch.float32 or not x.is_cuda:
+            raise ValueError("x must be an fp32 CUDA tensor")
+        ys = [torch.empty_like(x) for _ in range(3)]
+        with _on(x.device):
+            _check(self.lib.attn_selftest_exp2(_ptr(x), *(_ptr(y) for y in ys), x.numel(),
+                                               _stream(x.device)))
+        return tuple(ys)
 
     def selftest_wait_timeout(self, timeout_ns, device=None):
         dev = torch.device("cuda", torch.cuda.current_device()) if device is None else device

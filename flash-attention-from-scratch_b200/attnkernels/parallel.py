@@ -51,8 +51,9 @@ def context_range(context_len: int, block_size: int, world: int, rank: int) -> t
     return min(context_len, b0 * block_size), min(context_len, b1 * block_size)
 
 
-def _gather_flat(buf: torch.Tensor, world: int, group) -> torch.Tensor:
-    out = torch.empty((world, buf.numel()), dtype=buf.dtype, device=buf.device)
+def _gather_flat(buf: torch.Tensor, world: int, group, out=None) -> torch.Tensor:
+    if out is None:
+        out = torch.empty((world, buf.numel()), dtype=buf.dtype, device=buf.device)
     if dist.get_backend(group) == "nccl":
         dist.all_gather_into_tensor(out, buf, group=group)
     else:
@@ -75,6 +76,13 @@ class ContextParallelDecode:
     chunks > 1 (CUDA tensors only) splits the batch: the all-gather of one
     chunk's partials runs on a side stream while the next chunk is decoded, so
     only the last chunk's exchange and the merges are exposed.
+
+    The partials buffer and the gather buffer of each chunk are kept between
+    calls (per device and shape), so a decode loop allocates nothing after its
+    first step. Reuse is ordered by the streams: a call's partials kernel is
+    enqueued on the compute stream after the previous call's merge, which
+    itself waited for that call's gather; and a gather waits for the compute
+    stream before it overwrites its buffer.
     """
 
     def __init__(self, group=None, partials_fn=None, merge_fn=None, chunks=1):
@@ -88,6 +96,7 @@ class ContextParallelDecode:
         self.merge_fn = merge_fn
         self.chunks = max(1, int(chunks))
         self._comm = {}
+        self._bufs = {}
 
     @staticmethod
     def _views(buf, rows_b, heads, d):
@@ -96,16 +105,31 @@ class ContextParallelDecode:
                 buf[..., rows * d: rows * (d + 1)].unflatten(-1, (rows_b, heads)),
                 buf[..., rows * (d + 1): rows * (d + 2)].unflatten(-1, (rows_b, heads)))
 
+    def _buffers(self, device, B, H, D, world, chunk, side_stream=None):
+        """(partials buffer, gather buffer) of one chunk, kept between calls."""
+        key = (str(device), B, H, D, world, chunk)
+        bufs = self._bufs.get(key)
+        if bufs is None:
+            # One fp32 buffer per rank: o [rows, D], m [rows], l [rows], padded to
+            # 16 bytes so every part's o rows stay 16-byte aligned after the gather.
+            stride = -(-(B * H * (D + 2)) // 4) * 4
+            buf = torch.empty(stride, dtype=torch.float32, device=device)
+            gathered = torch.empty((world, stride), dtype=torch.float32, device=device)
+            if side_stream is not None:
+                # Used on the side stream too: the allocator must not hand the
+                # memory out again before that stream is done with it.
+                buf.record_stream(side_stream)
+                gathered.record_stream(side_stream)
+            bufs = self._bufs[key] = (buf, gathered)
+        return bufs
+
     def _exchange(self, q, k_cache, v_cache, block_tables, context_lens, max_context_len,
-                  scale, partition_size, world):
+                  scale, partition_size, world, chunk=0, side_stream=None):
         B, H, D = q.shape
-        # One fp32 buffer per rank: o [rows, D], m [rows], l [rows], padded to
-        # 16 bytes so every part's o rows stay 16-byte aligned after the gather.
-        stride = -(-(B * H * (D + 2)) // 4) * 4
-        buf = torch.empty(stride, dtype=torch.float32, device=q.device)
+        buf, gathered = self._buffers(q.device, B, H, D, world, chunk, side_stream)
         self.partials_fn(q, k_cache, v_cache, block_tables, context_lens, max_context_len,
                          scale, partition_size, out=self._views(buf, B, H, D))
-        return buf
+        return buf, gathered
 
     def __call__(self, q, k_cache, v_cache, block_tables, context_lens, max_context_len,
                  scale=None, partition_size=None):
@@ -115,9 +139,9 @@ class ContextParallelDecode:
         B, H, D = q.shape
         nchunks = min(self.chunks, B) if q.is_cuda and not self.custom_merge else 1
         if nchunks == 1:
-            buf = self._exchange(q, k_cache, v_cache, block_tables, context_lens,
-                                 max_context_len, scale, partition_size, world)
-            gathered = _gather_flat(buf, world, self.group)
+            buf, gathered = self._exchange(q, k_cache, v_cache, block_tables, context_lens,
+                                           max_context_len, scale, partition_size, world)
+            _gather_flat(buf, world, self.group, out=gathered)
             return self.merge_fn(*self._views(gathered, B, H, D))
         compute = torch.cuda.current_stream(q.device)
         comm = self._comm.get(q.device)
@@ -127,14 +151,12 @@ class ContextParallelDecode:
         pending = []
         for c in range(nchunks):
             b0, b1 = shard_range(B, nchunks, c)
-            buf = self._exchange(q[b0:b1], k_cache, v_cache, block_tables[b0:b1],
-                                 context_lens[b0:b1], max_context_len, scale, partition_size,
-                                 world)
+            buf, gathered = self._exchange(q[b0:b1], k_cache, v_cache, block_tables[b0:b1],
+                                           context_lens[b0:b1], max_context_len, scale,
+                                           partition_size, world, chunk=c, side_stream=comm)
             comm.wait_stream(compute)
             with torch.cuda.stream(comm):
-                gathered = _gather_flat(buf, world, self.group)
-            buf.record_stream(comm)
-            gathered.record_stream(compute)
+                _gather_flat(buf, world, self.group, out=gathered)
             pending.append((b0, b1, gathered))
         compute.wait_stream(comm)
         for b0, b1, gathered in pending:

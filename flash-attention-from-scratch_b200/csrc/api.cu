@@ -2,6 +2,9 @@
 // conditions, per-device state (SM count, address of the device status word),
 // and dispatch to the launchers. No entry point allocates device memory or
 // synchronises the host, except attn_device_status which reads the status word.
+// The library's own device memory is two module globals, resident on every GPU
+// where its kernels are loaded: the status word below and the 32 MiB scratch
+// array of attn_paged_decode_noalloc (csrc/decode.cu).
 #include <cstdarg>
 #include <cstdio>
 #include <mutex>
@@ -323,6 +326,20 @@ int attn_selftest_wait_timeout(uint64_t timeout_ns, void* stream) {
   return ATTN_OK;
 }
 
+int attn_selftest_exp2(const float* x, float* y_poly, float* y_mufu, float* y_lib, int64_t n,
+                       void* stream) {
+  if (x == nullptr || y_poly == nullptr || y_mufu == nullptr || y_lib == nullptr)
+    return fail(ATTN_ERR_INVALID, "selftest_exp2: null pointer");
+  if (n < 0 || n > (int64_t(1) << 31))
+    return fail(ATTN_ERR_INVALID, "selftest_exp2: n must be in [0, 2^31]");
+  if (n == 0) return ATTN_OK;
+  LaunchCtx ctx;
+  int rc = device_ctx(static_cast<cudaStream_t>(stream), &ctx);
+  if (rc != ATTN_OK) return rc;
+  cudaError_t e = launch_selftest_exp2(x, y_poly, y_mufu, y_lib, n, ctx);
+  if (e != cudaSuccess) return cuda_fail(e, "selftest_exp2 launch");
+  return ATTN_OK;
+}
 
 int attn_paged_decode_noalloc(const void* q, const void* k_cache, const void* v_cache,
                               const int32_t* block_tables, const int32_t* context_lens, void* out,

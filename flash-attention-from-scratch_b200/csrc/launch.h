@@ -62,6 +62,11 @@ cudaError_t launch_merge(const float* o_parts, const float* m_parts, const float
 
 cudaError_t launch_selftest_wait(unsigned long long timeout_ns, const LaunchCtx& ctx);
 
+// The prefill softmax's exponentials on n inputs: FMA-pipe polynomial, MUFU
+// ex2.approx and exp2f (fp32 device arrays of n elements each).
+cudaError_t launch_selftest_exp2(const float* x, float* y_poly, float* y_mufu, float* y_lib,
+                                int64_t n, const LaunchCtx& ctx);
+
 // Size of the fixed device array that attn_paged_decode_noalloc uses as its
 // split-K scratch (32 MiB per device that loads the library).
 constexpr size_t kDecodeStaticScratchBytes = size_t(32) << 20;

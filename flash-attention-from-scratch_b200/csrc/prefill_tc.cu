@@ -53,17 +53,19 @@ constexpr int kBM = 128;                   // query rows per tile (MMA M)
 constexpr int kBN = 128;                   // key rows per tile
 constexpr float kRescaleThreshold = 8.0f;  // log2 units: rescale O when m grows by > 2^8
 // Of the 128 exponentials per row, how many run on the FMA pipe (a compile-time
-// tuning constant; the rest use the MUFU).
+// tuning constant, a multiple of 4 up to 128; the rest use the MUFU).
 #ifndef FAB_POLY_COLS
 #define FAB_POLY_COLS 16
 #endif
 constexpr int kPolyCols = FAB_POLY_COLS;
-// 1: exponentials as ex2.approx.f16x2 (two per MUFU op); 0: fp32 ex2 (+ polynomial).
-#ifndef FAB_EXP_HALF2
-#define FAB_EXP_HALF2 0
+static_assert(kPolyCols % 4 == 0 && kPolyCols <= kBN, "pairs of columns in each half");
+// Register split of setmaxnreg (tuning constants; see TcCfg).
+#ifndef FAB_CONTROL_REGS
+#define FAB_CONTROL_REGS 64
 #endif
-constexpr bool kExpHalf2 = FAB_EXP_HALF2 != 0;
-static_assert(kPolyCols % 2 == 0 && kPolyCols <= kBN, "pairs of columns");
+#ifndef FAB_SOFTMAX_REGS
+#define FAB_SOFTMAX_REGS 216
+#endif
 
 // Sites reported in the status word when a wait times out.
 enum : unsigned int {
@@ -111,8 +113,8 @@ struct TcCfg {
   // rounded down to 8); the control warpgroup drops to 64 and the softmax
   // warpgroups rise to 216: 128 * 64 + 256 * 216 <= 384 * 168.
   static constexpr int LAUNCH_REGS = 168;
-  static constexpr int CONTROL_REGS = 64;
-  static constexpr int SOFTMAX_REGS = 216;
+  static constexpr int CONTROL_REGS = FAB_CONTROL_REGS;
+  static constexpr int SOFTMAX_REGS = FAB_SOFTMAX_REGS;
   static_assert(NQ == 2, "the register split assumes two softmax warpgroups");
   static_assert(128 * CONTROL_REGS + 256 * SOFTMAX_REGS <= THREADS * LAUNCH_REGS, "register split");
   static constexpr int O_COL = NQ * kBN;  // first O column; S_i at i * kBN
@@ -455,26 +457,27 @@ __global__ void __launch_bounds__(TcCfg<D, NQ>::THREADS, 1)
         // scale is folded into the exponent's FMA; otherwise the row is
         // scaled first.
         uint32_t sr[kBN];
-        float cs = p.scale_log2;
+        const float cs = p.scale_log2 > 0.f ? p.scale_log2 : 1.f;
         const int k0 = j * kBN;
-        auto load_row = [&]() {
-          tmem_ld128_wait(t_s, sr);
-          cs = p.scale_log2;
-          if (cs <= 0.f) {
+        const bool masked = (p.causal && j == qt) || k0 + kBN > p.n;
+        // Columns [lo, hi) of the scores just loaded: scaled when the scale is
+        // not positive, keys past the causal diagonal or the sequence end -inf.
+        auto fix_cols = [&](int lo, int hi) {
+          if (p.scale_log2 <= 0.f) {
+            const uint64_t sc2 = f2_pack(p.scale_log2, p.scale_log2);
 #pragma unroll
-            for (int c = 0; c < kBN; c += 2) {
+            for (int c = lo; c < hi; c += 2) {
               float a, b;
-              f2_unpack(f2_mul(f2_pack(__uint_as_float(sr[c]), __uint_as_float(sr[c + 1])),
-                               f2_pack(cs, cs)), a, b);
+              f2_unpack(f2_mul(f2_pack(__uint_as_float(sr[c]), __uint_as_float(sr[c + 1])), sc2),
+                        a, b);
               sr[c] = __float_as_uint(a);
               sr[c + 1] = __float_as_uint(b);
             }
-            cs = 1.f;
           }
-          if ((p.causal && j == qt) || k0 + kBN > p.n) {
+          if (masked) {
             const int lim = p.causal ? min(q_row + 1, p.n) : p.n;  // keys [0, lim) are visible
 #pragma unroll
-            for (int c = 0; c < kBN; ++c)
+            for (int c = lo; c < hi; ++c)
               if (k0 + c >= lim) sr[c] = __float_as_uint(-INFINITY);
           }
         };
@@ -493,48 +496,23 @@ __global__ void __launch_bounds__(TcCfg<D, NQ>::THREADS, 1)
         auto exp_pair = [&](int c) {  // pair c: scores 2c, 2c+1 -> packed fp16 in sr[c]
           const uint64_t x =
               f2_fma(f2_pack(__uint_as_float(sr[2 * c]), __uint_as_float(sr[2 * c + 1])), cs2, nm2);
-          if constexpr (kExpHalf2) {
-            // One MUFU op for the pair, in fp16 (the precision P is kept in);
-            // the row sum adds the same rounded values in fp32.
+          uint64_t pr;
+          if ((2 * c) % (kBN / 2) < kBN / 2 - kPolyCols / 2) {
             float a, b;
             f2_unpack(x, a, b);
-            const uint32_t ph = fast_exp2_h2(pack_half2(a, b));
-            const float2 pf = __half22float2(*reinterpret_cast<const __half2*>(&ph));
-            if (c & 1) rs1 = f2_add(rs1, f2_pack(pf.x, pf.y)); else rs0 = f2_add(rs0, f2_pack(pf.x, pf.y));
-            sr[c] = ph;
+            pr = f2_pack(fast_exp2(a), fast_exp2(b));
           } else {
-            uint64_t pr;
-            if ((2 * c) % (kBN / 2) < kBN / 2 - kPolyCols / 2) {
-              float a, b;
-              f2_unpack(x, a, b);
-              pr = f2_pack(fast_exp2(a), fast_exp2(b));
-            } else {
-              pr = f2_exp2_poly(x);
-            }
-            if (c & 1) rs1 = f2_add(rs1, pr); else rs0 = f2_add(rs0, pr);
-            float a, b;
-            f2_unpack(pr, a, b);
-            sr[c] = pack_half2(a, b);
+            pr = f2_exp2_poly(x);
           }
+          if (c & 1) rs1 = f2_add(rs1, pr); else rs0 = f2_add(rs0, pr);
+          float a, b;
+          f2_unpack(pr, a, b);
+          sr[c] = pack_half2(a, b);
         };
-        float mt[8];
-        load_row();
-#pragma unroll
-        for (int a = 0; a < 8; ++a)
-          mt[a] = fmax3(__uint_as_float(sr[3 * a]), __uint_as_float(sr[3 * a + 1]),
-                        __uint_as_float(sr[3 * a + 2]));
-#pragma unroll
-        for (int c = 24; c < kBN; c += 2)
-          mt[(c / 2) & 7] = fmax3(mt[(c / 2) & 7], __uint_as_float(sr[c]), __uint_as_float(sr[c + 1]));
-        const float m_new =
-            fmaxf(m, fmax3(fmax3(mt[0], mt[1], mt[2]), fmax3(mt[3], mt[4], mt[5]),
-                           fmaxf(mt[6], mt[7])) * cs);
-        if (j == 0) {
-          m = m_new;
-        } else if (__any_sync(0xffffffffu, m_new > m + kRescaleThreshold)) {
-          // Rescale O to the new max. O_i already holds P_{j-1} V: the MMAs of
-          // one thread complete in order, and S_i(j), whose completion this
-          // thread waited for, was issued after P_{j-1} V.
+        // O and l to a new running max. O_i already holds P_{j-1} V: the MMAs
+        // of one thread complete in order, and S_i(j), whose completion this
+        // thread waited for, was issued after P_{j-1} V.
+        auto rescale = [&](float m_new) {
           const float alpha = fast_exp2(m - m_new);
 #pragma unroll
           for (int c0 = 0; c0 < D; c0 += 32) {
@@ -553,10 +531,30 @@ __global__ void __launch_bounds__(TcCfg<D, NQ>::THREADS, 1)
           tmem_st_wait();
           l *= alpha;
           m = m_new;
-        }
-        start_exps();
+        };
+        tmem_ld128_wait(t_s, sr);
+        fix_cols(0, kBN);
+        {
+          // The row max (eight 3-input max chains), then O and l rescaled if it
+          // grew by more than kRescaleThreshold.
+          float mt[8];
 #pragma unroll
-        for (int c = 0; c < kBN / 4; ++c) exp_pair(c);
+          for (int a = 0; a < 8; ++a)
+            mt[a] = fmax3(__uint_as_float(sr[3 * a]), __uint_as_float(sr[3 * a + 1]),
+                          __uint_as_float(sr[3 * a + 2]));
+#pragma unroll
+          for (int c = 24; c < kBN; c += 2)
+            mt[(c / 2) & 7] = fmax3(mt[(c / 2) & 7], __uint_as_float(sr[c]), __uint_as_float(sr[c + 1]));
+          const float m_new = fmaxf(
+              m, fmax3(fmax3(mt[0], mt[1], mt[2]), fmax3(mt[3], mt[4], mt[5]), fmaxf(mt[6], mt[7])) * cs);
+          if (j == 0)
+            m = m_new;
+          else if (__any_sync(0xffffffffu, m_new > m + kRescaleThreshold))
+            rescale(m_new);
+          start_exps();
+#pragma unroll
+          for (int c = 0; c < kBN / 4; ++c) exp_pair(c);
+        }
         tmem_st32<0>(t_s, sr);
         tmem_st_wait();
         tc_fence_before();
@@ -661,6 +659,28 @@ cudaError_t launch_tc(const TcParams& prm, int64_t bh, const LaunchCtx& ctx) {
   return cudaGetLastError();
 }
 
+// Evaluates the exponentials the softmax uses, for the tests: y_poly[i] =
+// f2_exp2_poly (FMA pipe), y_mufu[i] = ex2.approx.ftz, y_lib[i] = exp2f, each
+// of x[i]. One thread per pair of inputs, as the kernel evaluates them.
+__global__ void exp2_selftest_kernel(const float* __restrict__ x, float* __restrict__ y_poly,
+                                     float* __restrict__ y_mufu, float* __restrict__ y_lib,
+                                     int64_t n) {
+  const int64_t i = 2 * (static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x);
+  if (i >= n) return;
+  const bool pair = i + 1 < n;
+  const float a = x[i], b = pair ? x[i + 1] : x[i];
+  float pa, pb;
+  f2_unpack(f2_exp2_poly(f2_pack(a, b)), pa, pb);
+  y_poly[i] = pa;
+  y_mufu[i] = fast_exp2(a);
+  y_lib[i] = exp2f(a);
+  if (pair) {
+    y_poly[i + 1] = pb;
+    y_mufu[i + 1] = fast_exp2(b);
+    y_lib[i + 1] = exp2f(b);
+  }
+}
+
 }  // namespace
 
 cudaError_t launch_flash_tc(const void* q, const void* k, const void* v, void* o, int64_t bh,
@@ -690,6 +710,14 @@ cudaError_t launch_flash_tc(const void* q, const void* k, const void* v, void* o
   prm.scale_log2 = scale * kLog2e;
   if (d == 64) return launch_tc<64, kNQ>(prm, bh, ctx);
   return launch_tc<128, kNQ>(prm, bh, ctx);
+}
+
+cudaError_t launch_selftest_exp2(const float* x, float* y_poly, float* y_mufu, float* y_lib,
+                                int64_t n, const LaunchCtx& ctx) {
+  const int64_t pairs = (n + 1) / 2;
+  const unsigned grid = static_cast<unsigned>((pairs + 255) / 256);
+  exp2_selftest_kernel<<<grid, 256, 0, ctx.stream>>>(x, y_poly, y_mufu, y_lib, n);
+  return cudaGetLastError();
 }
 
 }  // namespace fab

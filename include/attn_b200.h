@@ -13,7 +13,12 @@
  *
  * The caller owns every buffer, outputs included. Kernels that need scratch
  * memory take a `workspace` pointer whose minimum size a *_workspace_bytes()
- * query returns; the library itself never allocates device memory.
+ * query returns; no entry point allocates device memory. The library does
+ * hold two fixed device arrays of its own: the 8-byte status word, and the
+ * 32 MiB scratch array of attn_paged_decode_noalloc. Both are module globals,
+ * so every GPU on which the library's kernels are loaded (the CUDA runtime
+ * loads them on the first call that uses that device) holds them until the
+ * process exits, whether or not the no-alloc entry point is ever called.
  *
  * Return value: ATTN_OK (0) or an attn_status_t error code; the message of
  * the last error on the calling thread is in attn_last_error(). Argument
@@ -204,6 +209,17 @@ int attn_device_status(uint32_t* code, uint32_t* site);
  * reports ATTN_DEVICE_WAIT_TIMEOUT. No counterpart in the reference.
  */
 int attn_selftest_wait_timeout(uint64_t timeout_ns, void* stream);
+
+/*
+ * Evaluate the exponentials of the prefill kernel's softmax on n fp32 inputs
+ * (device arrays of n elements): y_poly = the FMA-pipe 2^x (range reduction plus
+ * a degree-3 minimax polynomial, relative error <= 7.5e-5 for x in
+ * [-125.99, 127); inputs below -126 and -inf give a value below 2^-125),
+ * y_mufu = ex2.approx.ftz.f32, y_lib = exp2f. For the tests; no counterpart in
+ * the reference, whose kernels call exp2f.
+ */
+int attn_selftest_exp2(const float* x, float* y_poly, float* y_mufu, float* y_lib, int64_t n,
+                       void* stream);
 
 #ifdef __cplusplus
 }

@@ -74,6 +74,12 @@ def _worker(rank, world, port, ctx, fail_rank, result_path):
         out = run(q, kc, vc, bt_local, lens_local, int(lens_local.max()))
         full = ref.paged_decode_fp32(q, kc, vc, tables, lens)
         err = (out - full).abs().max().item()
+        # A second step with another query reuses the kept buffers.
+        q2 = torch.randn(len(ctx), hq, d).half()
+        out2 = run(q2, kc, vc, bt_local, lens_local, int(lens_local.max()))
+        full2 = ref.paged_decode_fp32(q2, kc, vc, tables, lens)
+        err = max(err, (out2 - full2).abs().max().item())
+        assert len(run._bufs) == 1
         Path(result_path + f".{rank}").write_text(f"ok {err}")
     except RuntimeError as e:  # the collective failed: expected when a peer left
         Path(result_path + f".{rank}").write_text(f"error {type(e).__name__}")

@@ -1,10 +1,17 @@
 """Prefill attention on the GPU vs the fp32 CPU oracle.
 
 The first group restates the reference's tests/test_prefill.py cases (all four
-variants, its ATOL); the second holds the tcgen05 kernel to this build's
-tolerance (max-abs 2e-3 AND mean-abs 1e-4 on fp16 outputs) on the golden
-fixtures and on the BASELINE shapes at full size, checked on sampled heads and
-rows (slicing the oracle by head or by query rows is exact).
+variants); each case asserts the reference's own ATOL and this build's
+tolerance, max-abs 2e-3 AND mean-abs 1e-4 on fp16 outputs. The second group
+holds the kernels to that tolerance on the golden fixtures and on the BASELINE
+shapes at full size, checked on sampled heads and rows (slicing the oracle by
+head or by query rows is exact).
+
+One case has a wider mean-abs bound, for a stated reason: with scores of std 6
+(test_large_logits, the large-logit fixture) the outputs are close to single
+rows of v, |o| up to ~4, and rounding the exact fp32 answer to fp16 alone
+already leaves a mean-abs error of 1.02e-4 (1.04e-4 at d 64) on those inputs;
+there the bound is 2e-3 max-abs and 2e-4 mean-abs.
 """
 from pathlib import Path
 
@@ -21,6 +28,7 @@ pytestmark = pytest.mark.gpu
 ATOL = 5e-3          # the reference's prefill tolerance (tests/test_prefill.py:14)
 MAX_ABS = 2e-3       # this build's tolerance, max-abs ...
 MEAN_ABS = 1e-4      # ... and mean-abs, on fp16 outputs
+LARGE_LOGIT_MEAN_ABS = 2e-4  # fp16 rounding of the exact answer alone is 1.0e-4 there
 GOLDEN = Path(__file__).resolve().parent / "golden"
 
 VARIANTS = {
@@ -53,6 +61,7 @@ def test_matches_fp32(variant, causal, d, n):
     assert out.shape == q.shape and out.dtype == torch.float16
     assert torch.isfinite(out).all()
     assert max_err(out, ref) < ATOL
+    assert max_err(out, ref) < MAX_ABS and mean_err(out, ref) < MEAN_ABS
 
 
 @pytest.mark.parametrize("variant", ["simt", "wmma32", "wmma64"])
@@ -61,7 +70,9 @@ def test_matches_fp32(variant, causal, d, n):
 def test_long_sequence(variant, causal, d):
     q, k, v = rand_qkv(1, 2, 2048 + 7, d)
     out = VARIANTS[variant](q, k, v, causal)
-    assert max_err(out, oracle(q, k, v, causal)) < ATOL
+    ref = oracle(q, k, v, causal)
+    assert max_err(out, ref) < ATOL
+    assert max_err(out, ref) < MAX_ABS and mean_err(out, ref) < MEAN_ABS
 
 
 @pytest.mark.parametrize("variant", list(VARIANTS))
@@ -71,7 +82,9 @@ def test_large_logits(variant, d):
     q, k, v = rand_qkv(1, 2, 300, d, q_scale=6.0)
     out = VARIANTS[variant](q, k, v, True)
     assert torch.isfinite(out).all()
-    assert max_err(out, oracle(q, k, v, True)) < 2 * ATOL
+    ref = oracle(q, k, v, True)
+    assert max_err(out, ref) < 2 * ATOL
+    assert max_err(out, ref) < MAX_ABS and mean_err(out, ref) < LARGE_LOGIT_MEAN_ABS
 
 
 def test_causal_first_row_is_v0():
@@ -87,6 +100,8 @@ def test_matches_sdpa(variant):
     out = VARIANTS[variant](q, k, v, True)
     sdpa = torch.nn.functional.scaled_dot_product_attention(q, k, v, is_causal=True)
     assert max_err(out, sdpa) < ATOL
+    ref = oracle(q, k, v, True)
+    assert max_err(out, ref) < MAX_ABS and mean_err(out, ref) < MEAN_ABS
 
 
 def test_rejects_bad_input():
@@ -104,17 +119,17 @@ def test_rejects_bad_input():
 
 
 @pytest.mark.parametrize("path", sorted(GOLDEN.glob("prefill_*.npz")), ids=lambda p: p.stem)
-@pytest.mark.parametrize("variant", ["wmma64", "simt"])
+@pytest.mark.parametrize("variant", list(VARIANTS))
 def test_golden_fixtures(path, variant):
-    """Inputs and outputs produced by the reference's own oracle."""
+    """Inputs and outputs produced by the reference's own oracle, every variant."""
     with np.load(path) as z:
         q, k, v = (torch.from_numpy(z[n]).cuda() for n in "qkv")
         want = torch.from_numpy(z["out"])
         causal = bool(z["causal"])
     out = VARIANTS[variant](q, k, v, causal)
-    tol = 2 if "large_logits" in path.stem else 1
-    assert max_err(out, want) < tol * MAX_ABS
-    assert mean_err(out, want) < tol * MEAN_ABS
+    mean_tol = LARGE_LOGIT_MEAN_ABS if "large_logits" in path.stem else MEAN_ABS
+    assert max_err(out, want) < MAX_ABS
+    assert mean_err(out, want) < mean_tol
 
 
 @pytest.mark.parametrize("d,n", [(128, 4096), (64, 4096), (128, 4095)])
@@ -183,17 +198,18 @@ def test_tile_edges(n, causal):
 
 def test_scale_argument():
     q, k, v = rand_qkv(1, 2, 200, 64)
-    for scale in (0.05, 0.3):
+    for scale in (0.05, 0.3, -0.1):
         out = ak.flash_attention(q, k, v, causal=True, scale=scale)
         ref = attention_fp32(q.cpu(), k.cpu(), v.cpu(), True, scale=scale)
-        assert max_err(out, ref) < MAX_ABS
+        assert max_err(out, ref) < MAX_ABS and mean_err(out, ref) < MEAN_ABS
 
 
 def test_non_contiguous_inputs_are_made_contiguous():
     q, k, v = rand_qkv(2, 64, 4, 128)
     qt, kt, vt = (t.transpose(1, 2) for t in (q, k, v))  # [2, 4, 64, 128] views
     out = ak.flash_attention(qt, kt, vt, causal=True)
-    assert max_err(out, oracle(qt, kt, vt, True)) < MAX_ABS
+    ref = oracle(qt, kt, vt, True)
+    assert max_err(out, ref) < MAX_ABS and mean_err(out, ref) < MEAN_ABS
 
 
 def test_deterministic():
