@@ -304,6 +304,29 @@ def timed(fn, steps, warmup, d: Dist, spin_s=0.0, per_rank=None):
     return d.max(mine)
 
 
+def timed_each(fn, reps, warmup=1, flush_bytes=256 << 20, device=None):
+    """Per-call device times (ms) of `reps` calls of fn, each on a cold L2: a
+    buffer larger than L2 (126 MB) is written before every call, outside the
+    CUDA events that bracket the call on the current stream."""
+    dev = torch.device("cuda", torch.cuda.current_device()) if device is None else device
+    flush = torch.empty(flush_bytes, dtype=torch.uint8, device=dev)
+    stream = torch.cuda.current_stream(dev)
+    for _ in range(warmup):
+        fn()
+    out = []
+    for _ in range(reps):
+        flush.zero_()
+        start = torch.cuda.Event(enable_timing=True)
+        end = torch.cuda.Event(enable_timing=True)
+        start.record(stream)
+        fn()
+        end.record(stream)
+        end.synchronize()
+        out.append(start.elapsed_time(end))
+    del flush
+    return out
+
+
 class _E2EPipeline:
     """Pipelined end-to-end steps: host inputs -> device (stream 1), op (stream 2),
     output -> host (stream 3), with two device buffer sets so that consecutive

@@ -26,23 +26,25 @@ def test_decode_checks_match_oracle():
                                                 device="cpu", extra_blocks=2)
     q = torch.randn(3, 8, 32)
     want = ref.paged_decode_fp32(q, kc, vc, tables, lens)
-    row0 = bench_sweep.decode_row0_fp32(q, kc, vc, tables, ctx[0])
+    row0 = bench_sweep.decode_fp32_first(q, kc, vc, tables, ctx[0])
     assert (row0 - want[0]).abs().max().item() < 1e-5
     nblk = -(-max(ctx) // 16)
-    got = bench_sweep.gather_sdpa(q, kc, vc, tables, nblk, lens)
+    got = bench_sweep.gather_then_sdpa(q, kc, vc, tables, nblk, lens)
     assert (got - want).abs().max().item() < 1e-5
+    assert torch.equal(bench_sweep.contiguous_kv(kc, tables, nblk),
+                       ref.gather_kv(kc, tables, nblk))
 
 
 def test_kv_bytes_convention():
     # K and V, fp16, 8 kv heads of 128: the reference's bench/bench.py:199-200.
-    assert bench_sweep.kv_bytes([1024, 2048]) == 3072 * 8 * 128 * 4
+    assert bench_sweep.decode_kv_bytes([1024, 2048]) == 3072 * 8 * 128 * 4
 
 
 def test_report_renders_every_section():
     meta = {"gpu": "NVIDIA B200", "sm": "10.0", "sm_count": 148, "memory_gb": 178.4,
             "torch": "2.11", "cuda": "12.8", "nvidia_smi": "NVIDIA B200, 580.159, 1965, 3996",
-            "date": "now", "roofs": {"copy_gbps": 6500.0, "fp16_gemm_tflops": 1500.0},
-            "measured_peaks": {"hbm_gbs": 6536.0, "tflops": 1644.0, "source": "MEASURED_PEAKS.json"},
+            "date": "now", "timing": "events per call",
+            "measured_peaks": {"hbm_gbs": 6536.0, "tflops": 1644.0, "source": "measured"},
             "sdpa_backends": {"FLASH_ATTENTION": "ok", "MATH": "unavailable: x"}}
     res = []
     for impl in ("sdpa", "flash_wmma_bn64"):
@@ -70,4 +72,5 @@ def test_report_renders_every_section():
                   "Split-K partition size", "Ragged batch: 3 sequences"):
         assert title in text, title
     assert "| 4096 | 4 | 900.00 | 900.00 |" in text
-    assert "| 1 | 32768 | 256 | 128 | 1024 | 0.0500 | 3000.0 |" in text
+    assert "| 1 | 32768 | 256 | 128 | 1024 | 0.0500 | 3000.0 | 0.400 |" in text
+    assert "| 128 | True | 4096 | 4 | 0.550 |" in text
