@@ -695,6 +695,14 @@ def bench_long_context(args, d: Dist, peaks, peak_src, traffic):
         "clocks": clk.summary(),
         "gpu_launches": launches * args.steps}
     if d.world > 1:
+        # The same step without the exchange: this rank's partials alone (decode kernel +
+        # local split-K merge), to name what the exchange and the merge across ranks add.
+        partials = lambda: ak.paged_decode_partials(q, kc, vc, tables, lens, t1 - t0,  # noqa: E731
+                                                    partition_size=part)
+        ms_local = timed(partials, args.steps, args.warmup, d)
+        out["config5_decode"]["local_partials_ms_per_step"] = round(ms_local / args.steps, 4)
+        out["config5_decode"]["exchange_and_merge_ms_per_step"] = round(
+            (ms - ms_local) / args.steps, 4)
         out["config5_decode"]["exchange"] = (
             f"NCCL all_gather_into_tensor of {c['batch'] * c['heads'] * (c['head_dim'] + 2) * 4} "
             f"bytes per rank, then the merge kernel; batch cut into "

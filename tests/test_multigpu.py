@@ -65,10 +65,16 @@ def _worker(rank, world, port, result_path):
             sub.append(t1 - t0)
         bt_local = torch.stack(rows)
         lens_local = torch.tensor(sub, dtype=torch.int32, device=dev)
-        out = ContextParallelDecode()(q, kc, vc, bt_local, lens_local, max(1, max(sub)),
-                                      partition_size=512)
+        cp = ContextParallelDecode()
+        out = cp(q, kc, vc, bt_local, lens_local, max(1, max(sub)), partition_size=512)
         full = ak.paged_decode(q, kc, vc, tables, lens, max(ctx), partition_size=512)
         lines.append(f"decode {(out.float() - full.float()).abs().max().item()}")
+        # A second step reuses the exchange buffers kept by the first.
+        q2 = torch.randn(q.shape, generator=torch.Generator(device=dev).manual_seed(18),
+                         device=dev).half()
+        out_b = cp(q2, kc, vc, bt_local, lens_local, max(1, max(sub)), partition_size=512)
+        full_b = ak.paged_decode(q2, kc, vc, tables, lens, max(ctx), partition_size=512)
+        lines.append(f"second {(out_b.float() - full_b.float()).abs().max().item()}")
         # The batch in chunks, exchange of one chunk overlapping the next one's decode.
         out2 = ContextParallelDecode(chunks=3)(q, kc, vc, bt_local, lens_local, max(1, max(sub)),
                                                partition_size=512)
@@ -107,5 +113,6 @@ def test_context_parallel_decode_two_gpus(tmp_path):
         assert "error" not in text, text
         vals = dict(line.split() for line in text.splitlines())
         assert float(vals["decode"]) < MAX_ABS, (r, text)
+        assert float(vals["second"]) < MAX_ABS, (r, text)
         assert float(vals["chunked"]) < MAX_ABS, (r, text)
         assert float(vals["prefill"]) == 0.0, (r, text)
