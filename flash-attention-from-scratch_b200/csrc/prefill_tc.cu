@@ -545,7 +545,7 @@ __global__ void __launch_bounds__(TcCfg<D, NQ>::THREADS, 1)
             auto fix_cols = [&](int lo, int hi) {
               if (p.scale_log2 <= 0.f) {
                 const uint64_t sc2 = f2_pack(p.scale_log2, p.scale_log2);
-    #pragma unroll
+#pragma unroll
                 for (int c = lo; c < hi; c += 2) {
                   float a, b;
                   f2_unpack(f2_mul(f2_pack(__uint_as_float(sr[c]), __uint_as_float(sr[c + 1])), sc2),
@@ -556,7 +556,7 @@ __global__ void __launch_bounds__(TcCfg<D, NQ>::THREADS, 1)
               }
               if (masked) {
                 const int lim = p.causal ? min(q_row + 1, p.n) : p.n;  // keys [0, lim) are visible
-    #pragma unroll
+#pragma unroll
                 for (int c = lo; c < hi; ++c)
                   if (k0 + c >= lim) sr[c] = __float_as_uint(-INFINITY);
               }
@@ -594,11 +594,11 @@ __global__ void __launch_bounds__(TcCfg<D, NQ>::THREADS, 1)
             // thread waited for, was issued after P_{j-1} V.
             auto rescale = [&](float m_new) {
               const float alpha = fast_exp2(m - m_new);
-    #pragma unroll
+#pragma unroll
               for (int c0 = 0; c0 < D; c0 += 32) {
                 uint32_t o[32];
                 tmem_ld32_wait(t_o + c0, o);
-    #pragma unroll
+#pragma unroll
                 for (int e = 0; e < 32; e += 2) {
                   float a, b;
                   f2_unpack(f2_mul(f2_pack(__uint_as_float(o[e]), __uint_as_float(o[e + 1])),
@@ -618,11 +618,11 @@ __global__ void __launch_bounds__(TcCfg<D, NQ>::THREADS, 1)
               // The row max (eight 3-input max chains), then O and l rescaled if it
               // grew by more than kRescaleThreshold.
               float mt[8];
-    #pragma unroll
+#pragma unroll
               for (int a = 0; a < 8; ++a)
                 mt[a] = fmax3(__uint_as_float(sr[3 * a]), __uint_as_float(sr[3 * a + 1]),
                               __uint_as_float(sr[3 * a + 2]));
-    #pragma unroll
+#pragma unroll
               for (int c = 24; c < kBN; c += 2)
                 mt[(c / 2) & 7] = fmax3(mt[(c / 2) & 7], __uint_as_float(sr[c]), __uint_as_float(sr[c + 1]));
               const float m_new = fmaxf(
@@ -632,7 +632,7 @@ __global__ void __launch_bounds__(TcCfg<D, NQ>::THREADS, 1)
               else if (__any_sync(0xffffffffu, m_new > m + kRescaleThreshold))
                 rescale(m_new);
               start_exps();
-    #pragma unroll
+#pragma unroll
               for (int c = 0; c < kBN / 4; ++c) exp_pair(c);
             }
             tmem_st32<0>(t_s, sr);
@@ -640,7 +640,7 @@ __global__ void __launch_bounds__(TcCfg<D, NQ>::THREADS, 1)
             tc_fence_before();
             __syncwarp();
             if (lane == 0) mbar_arrive(p_full + 2 * wg);
-    #pragma unroll
+#pragma unroll
             for (int c = kBN / 4; c < kBN / 2; ++c) exp_pair(c);
             tmem_st32<32>(t_s + 32, sr);
             tmem_st_wait();
