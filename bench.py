@@ -676,10 +676,12 @@ def bench_long_context(args, d: Dist, peaks, peak_src, traffic):
                                      partition_size=part)
         launches = 2
     else:
-        cp = parallel.ContextParallelDecode(chunks=args.cp_chunks)
+        cp = (parallel.ContextParallelDecode(exchange="peer") if args.cp_exchange == "peer"
+              else parallel.ContextParallelDecode(chunks=args.cp_chunks, exchange="nccl"))
         fn = lambda: cp(q, kc, vc, tables, lens, t1 - t0, partition_size=part)  # noqa: E731
-        # per chunk: decode kernel + local split-K merge + the merge across ranks
-        launches = 3 * min(args.cp_chunks, c["batch"])
+        # per chunk: decode kernel + local split-K merge + the merge across ranks (the
+        # peer exchange: decode + local merge + one exchange-and-merge kernel)
+        launches = 3 if args.cp_exchange == "peer" else 3 * min(args.cp_chunks, c["batch"])
     with NvmlClockSampler(d.device) as clk:
         ms = timed(fn, args.steps, args.warmup, d)
     total = kv_bytes([c["ctx"]] * c["batch"], c["kv_heads"], c["head_dim"])
@@ -703,11 +705,14 @@ def bench_long_context(args, d: Dist, peaks, peak_src, traffic):
         out["config5_decode"]["local_partials_ms_per_step"] = round(ms_local / args.steps, 4)
         out["config5_decode"]["exchange_and_merge_ms_per_step"] = round(
             (ms - ms_local) / args.steps, 4)
+        nbytes = c["batch"] * c["heads"] * (c["head_dim"] + 2) * 4
         out["config5_decode"]["exchange"] = (
-            f"NCCL all_gather_into_tensor of {c['batch'] * c['heads'] * (c['head_dim'] + 2) * 4} "
-            f"bytes per rank, then the merge kernel; batch cut into "
-            f"{min(args.cp_chunks, c['batch'])} chunk(s) whose exchanges overlap the next "
-            f"chunk's decode")
+            f"peer memory: each rank stores its {nbytes} bytes of partials into every peer over "
+            f"NVLink and raises a flag there; one kernel waits for the peers' flags and merges"
+            if args.cp_exchange == "peer" else
+            f"NCCL all_gather_into_tensor of {nbytes} bytes per rank, then the merge kernel; "
+            f"batch cut into {min(args.cp_chunks, c['batch'])} chunk(s) whose exchanges "
+            f"overlap the next chunk's decode")
     return out
 
 
@@ -900,6 +905,9 @@ def main():
     ap.add_argument("--spin", type=float, default=0.0,
                     help="seconds of untimed load before a timed region (default none: the "
                          "clocks are sampled during the timed steps themselves)")
+    ap.add_argument("--cp-exchange", choices=["nccl", "peer"], default="peer",
+                    help="how context-parallel decode exchanges its partials at N > 1: an NCCL "
+                         "all-gather + merge kernel, or one kernel over peer memory")
     ap.add_argument("--cp-chunks", type=int, default=1,
                     help="batch chunks of the context-parallel decode at N > 1 (each "
                          "chunk's exchange overlaps the next chunk's decode)")

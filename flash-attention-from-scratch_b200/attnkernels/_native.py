@@ -50,6 +50,8 @@ SIGNATURES = {
     "attn_device_status": (_int, [_u32p, _u32p]),
     "attn_selftest_wait_timeout": (_int, [ctypes.c_uint64, _vp]),
     "attn_selftest_exp2": (_int, [_vp, _vp, _vp, _vp, _i64, _vp]),
+    "attn_exchange_merge_partials": (_int, [ctypes.POINTER(_vp), ctypes.POINTER(_vp), _int, _int,
+                                            ctypes.c_uint32, _i64, _i64, _i64, _vp, _vp]),
 }
 
 ABI_VERSION = 1
@@ -228,6 +230,19 @@ class Extension:
                 _ptr(o_parts), _ptr(m_parts), _ptr(l_parts), int(num_parts), int(rows),
                 int(head_dim), int(o_part_stride), int(ml_part_stride), _ptr(out),
                 _stream(out.device)))
+        return out
+
+    def exchange_merge_partials(self, slot_ptrs, flag_ptrs, rank, epoch, rows, head_dim,
+                                slot_stride, out):
+        """attn_exchange_merge_partials: slot_ptrs / flag_ptrs are the device addresses
+        (ints) of every rank's receive area and flag words for this call."""
+        world = len(slot_ptrs)
+        slots = (_vp * world)(*slot_ptrs)
+        flags = (_vp * world)(*flag_ptrs)
+        with _on(out.device):
+            _check(self.lib.attn_exchange_merge_partials(
+                slots, flags, int(world), int(rank), int(epoch) & 0xFFFFFFFF, int(rows),
+                int(head_dim), int(slot_stride), _ptr(out), _stream(out.device)))
         return out
 
     # -------------------------------------------------------------- status

@@ -12,6 +12,11 @@ The reference is single-GPU; this module is the B200 box layer:
   (sequence, head) row over its range with paged_decode_partials, the states
   are all-gathered over NCCL (the only collective: B * H * (D + 2) fp32 per
   rank), and every rank merges them with merge_partials into the fp16 output.
+  With exchange="peer" the all-gather and the merge are one kernel instead
+  (attn_exchange_merge_partials): each rank pushes its partials into every
+  peer's receive area over NVLink (torch symmetric memory gives the peer
+  pointers), signals each peer with a flag, waits for the peers' flags and
+  merges; no collective launch.
 
 The compute steps are injectable so that the orchestration (packing, the
 collective, the merge layout) can be tested on CPU ranks with gloo and the CPU
@@ -61,6 +66,40 @@ def _gather_flat(buf: torch.Tensor, world: int, group, out=None) -> torch.Tensor
     return out
 
 
+class _PeerArea:
+    """Receive areas of the peer exchange for one (device, rows, head_dim): two
+    areas (alternated by call parity) of `world` slots, each slot o [rows][D],
+    m [rows], l [rows] fp32 padded to 16 bytes, then the flag words
+    [world][ceil(rows / 8)]; one symmetric allocation, rendezvoused over the group
+    so that every rank holds every rank's device addresses."""
+
+    def __init__(self, group, device, rows, d, world, rank):
+        import torch.distributed._symmetric_memory as symm_mem
+
+        self.rows, self.d, self.world, self.rank = rows, d, world, rank
+        self.stride = -(-(rows * (d + 2)) // 4) * 4
+        self.area_floats = world * self.stride
+        blocks = -(-rows // 8)
+        total = 2 * self.area_floats + world * blocks
+        group = group if group is not None else dist.group.WORLD
+        name = group.group_name
+        self.buf = symm_mem.empty(total, dtype=torch.float32, device=device)
+        self.buf.zero_()  # the flags start at 0
+        torch.cuda.synchronize(device)
+        handle = symm_mem.rendezvous(self.buf, name)
+        base = [int(x) for x in handle.buffer_ptrs]
+        self.handle = handle
+        self.slots = [[b + 4 * par * self.area_floats for b in base] for par in (0, 1)]
+        self.flags = [b + 4 * 2 * self.area_floats for b in base]
+        self.epoch = 0
+        dist.barrier(group)  # every rank's flags are zero before anyone signals
+
+    def own_slot(self, par):
+        """This rank's slot of its own receive area for call parity `par`."""
+        start = par * self.area_floats + self.rank * self.stride
+        return self.buf[start:start + self.stride]
+
+
 class ContextParallelDecode:
     """Decode with each sequence's context split across the ranks of `group`.
 
@@ -72,6 +111,11 @@ class ContextParallelDecode:
     partials_fn(q, kc, vc, bt, lens, max_len, scale, partition, out=(o, m, l))
     fills o [B, H, D], m and l [B, H] (fp32); merge_fn(o_parts, m_parts,
     l_parts) merges [P, B, H, D] / [P, B, H] views. Defaults: the CUDA kernels.
+
+    exchange="peer" (the default with the CUDA kernels and one chunk) replaces the
+    all-gather and the merge by attn_exchange_merge_partials over peer memory (see
+    the module doc); exchange="nccl" keeps the all-gather (and is what custom steps
+    or chunks use).
 
     chunks > 1 (CUDA tensors only) splits the batch: the all-gather of one
     chunk's partials runs on a side stream while the next chunk is decoded, so
@@ -85,7 +129,16 @@ class ContextParallelDecode:
     stream before it overwrites its buffer.
     """
 
-    def __init__(self, group=None, partials_fn=None, merge_fn=None, chunks=1):
+    def __init__(self, group=None, partials_fn=None, merge_fn=None, chunks=1, exchange=None):
+        if exchange is None:  # the fused peer kernel unless the steps are customised
+            custom = partials_fn is not None or merge_fn is not None or chunks != 1
+            exchange = "nccl" if custom else "peer"
+        if exchange not in ("nccl", "peer"):
+            raise ValueError(f"exchange must be 'nccl' or 'peer', got {exchange!r}")
+        if exchange == "peer" and (partials_fn is not None or merge_fn is not None or chunks != 1):
+            raise ValueError("exchange='peer' runs the CUDA kernels, in one chunk")
+        self.exchange = exchange
+        self._areas = {}
         self.group = group
         self.custom_merge = merge_fn is not None
         if partials_fn is None or merge_fn is None:
@@ -137,6 +190,9 @@ class ContextParallelDecode:
         if q.dim() == 4:
             q = q.reshape(q.shape[0], q.shape[1], q.shape[3])
         B, H, D = q.shape
+        if self.exchange == "peer" and q.is_cuda:
+            return self._peer_call(q, k_cache, v_cache, block_tables, context_lens,
+                                   max_context_len, scale, partition_size, world)
         nchunks = min(self.chunks, B) if q.is_cuda and not self.custom_merge else 1
         if nchunks == 1:
             buf, gathered = self._exchange(q, k_cache, v_cache, block_tables, context_lens,
@@ -162,3 +218,21 @@ class ContextParallelDecode:
         for b0, b1, gathered in pending:
             self.merge_fn(*self._views(gathered, b1 - b0, H, D), out=out[b0:b1])
         return out
+
+    def _peer_call(self, q, k_cache, v_cache, block_tables, context_lens, max_context_len,
+                   scale, partition_size, world):
+        from . import load_extension
+
+        B, H, D = q.shape
+        key = (str(q.device), B * H, D, world)
+        area = self._areas.get(key)
+        if area is None:
+            area = self._areas[key] = _PeerArea(self.group, q.device, B * H, D, world,
+                                                dist.get_rank(self.group))
+        area.epoch += 1
+        par = area.epoch & 1
+        self.partials_fn(q, k_cache, v_cache, block_tables, context_lens, max_context_len,
+                         scale, partition_size, out=self._views(area.own_slot(par), B, H, D))
+        out = torch.empty(B, H, D, dtype=torch.float16, device=q.device)
+        return load_extension().exchange_merge_partials(
+            area.slots[par], area.flags, area.rank, area.epoch, B * H, D, area.stride, out)

@@ -27,7 +27,7 @@ ROOT = PKG.parent
 CSRC = PKG / "csrc"
 BUILD = PKG / "_build"
 LIB = PKG / "attnkernels" / "libattn_b200.so"
-SOURCES = ["api.cu", "prefill_tc.cu", "prefill_simt.cu", "decode.cu"]
+SOURCES = ["api.cu", "prefill_tc.cu", "prefill_simt.cu", "decode.cu", "exchange.cu"]
 HEADERS = ["common.cuh", "launch.h"]
 ARCH = ["-gencode", "arch=compute_100a,code=sm_100a"]
 

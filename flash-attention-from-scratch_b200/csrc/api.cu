@@ -326,6 +326,37 @@ int attn_selftest_wait_timeout(uint64_t timeout_ns, void* stream) {
   return ATTN_OK;
 }
 
+int attn_exchange_merge_partials(float* const* slots, uint32_t* const* flags, int world, int rank,
+                                 uint32_t epoch, int64_t rows, int64_t head_dim,
+                                 int64_t slot_stride, void* out, void* stream) {
+  if (slots == nullptr || flags == nullptr || out == nullptr)
+    return fail(ATTN_ERR_INVALID, "exchange_merge_partials: null pointer");
+  if (world < 1 || world > kMaxPeers || rank < 0 || rank >= world)
+    return fail(ATTN_ERR_INVALID, "exchange_merge_partials: rank %d of world %d (at most %d)",
+                rank, world, kMaxPeers);
+  if (head_dim != 64 && head_dim != 128)
+    return fail(ATTN_ERR_UNSUPPORTED, "exchange_merge_partials: head_dim must be 64 or 128");
+  if (rows < 0 || rows > 0x7fffffffLL || slot_stride < rows * (head_dim + 2) ||
+      (slot_stride % 4) != 0)
+    return fail(ATTN_ERR_INVALID,
+                "exchange_merge_partials: slot_stride must hold rows * (head_dim + 2) floats "
+                "and be a multiple of 4");
+  for (int q = 0; q < world; ++q)
+    if (slots[q] == nullptr || flags[q] == nullptr || !aligned16(slots[q]))
+      return fail(ATTN_ERR_INVALID,
+                  "exchange_merge_partials: slot %d must be a 16-byte aligned pointer", q);
+  if (!aligned16(out))
+    return fail(ATTN_ERR_INVALID, "exchange_merge_partials: out must be 16-byte aligned");
+  if (rows == 0) return ATTN_OK;
+  LaunchCtx ctx;
+  int rc = device_ctx(static_cast<cudaStream_t>(stream), &ctx);
+  if (rc != ATTN_OK) return rc;
+  cudaError_t e = launch_exchange_merge(slots, flags, world, rank, epoch, rows,
+                                        static_cast<int>(head_dim), slot_stride, out, ctx);
+  if (e != cudaSuccess) return cuda_fail(e, "exchange_merge_partials launch");
+  return ATTN_OK;
+}
+
 int attn_selftest_exp2(const float* x, float* y_poly, float* y_mufu, float* y_lib, int64_t n,
                        void* stream) {
   if (x == nullptr || y_poly == nullptr || y_mufu == nullptr || y_lib == nullptr)

@@ -67,6 +67,16 @@ cudaError_t launch_selftest_wait(unsigned long long timeout_ns, const LaunchCtx&
 cudaError_t launch_selftest_exp2(const float* x, float* y_poly, float* y_mufu, float* y_lib,
                                 int64_t n, const LaunchCtx& ctx);
 
+// Most ranks attn_exchange_merge_partials takes.
+constexpr int kMaxPeers = 16;
+
+// Context-parallel partials pushed to every peer over peer memory, then merged
+// (csrc/exchange.cu). slots[q] / flags[q]: rank q's receive area for this call
+// and its flag words, as device pointers valid on the current device.
+cudaError_t launch_exchange_merge(float* const* slots, unsigned int* const* flags, int world,
+                                  int rank, unsigned int epoch, int64_t rows, int d,
+                                  int64_t slot_stride, void* out, const LaunchCtx& ctx);
+
 // Size of the fixed device array that attn_paged_decode_noalloc uses as its
 // split-K scratch (32 MiB per device that loads the library).
 constexpr size_t kDecodeStaticScratchBytes = size_t(32) << 20;

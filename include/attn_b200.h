@@ -165,6 +165,34 @@ int attn_merge_partials(const float* o_parts, const float* m_parts, const float*
                         int64_t ml_part_stride, void* out, void* stream);
 
 /*
+ * Context-parallel decode across GPUs, the exchange and the merge in one
+ * kernel: pushes this rank's softmax partials to every peer over peer memory
+ * (NVLink stores), signals each peer, waits (time-limited) for every peer's
+ * partials, and merges them into fp16 rows (the merge of attn_merge_partials).
+ *
+ *   slots[q]   rank q's receive area for this call, a device pointer valid on
+ *              the current device (peer memory, e.g. torch symmetric memory):
+ *              `world` slots, `slot_stride` floats apart, each holding
+ *              o [rows][head_dim], m [rows], l [rows] fp32. Before the call,
+ *              this rank's own partials must be in slot `rank` of its own area
+ *              (attn_paged_decode_partials writing there).
+ *   flags[q]   rank q's flag words, uint32 [world][ceil(rows / 8)], zeroed once
+ *              before the first call.
+ *   epoch      1 on the first call, +1 on every call (the same on all ranks);
+ *              consecutive calls must alternate between two receive areas.
+ *   out        fp16 [rows][head_dim] on this rank.
+ * world <= 16; every rank calls with the same world, rows, head_dim, slot_stride
+ * and epoch. A peer that does not arrive within the wait limit leaves blocks of
+ * `out` unwritten and attn_device_status() reports ATTN_DEVICE_WAIT_TIMEOUT.
+ *
+ * No counterpart in the reference (single-GPU); it replaces the NCCL
+ * all-gather + attn_merge_partials pair of the context-parallel decode.
+ */
+int attn_exchange_merge_partials(float* const* slots, uint32_t* const* flags, int world, int rank,
+                                 uint32_t epoch, int64_t rows, int64_t head_dim,
+                                 int64_t slot_stride, void* out, void* stream);
+
+/*
  * attn_paged_decode without a workspace argument, for callers that cannot
  * allocate device memory where they run decode: a plugin inside a serving
  * framework that owns the whole device-memory pool and gives its plugins no

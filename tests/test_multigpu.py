@@ -65,7 +65,7 @@ def _worker(rank, world, port, result_path):
             sub.append(t1 - t0)
         bt_local = torch.stack(rows)
         lens_local = torch.tensor(sub, dtype=torch.int32, device=dev)
-        cp = ContextParallelDecode()
+        cp = ContextParallelDecode(exchange="nccl")
         out = cp(q, kc, vc, bt_local, lens_local, max(1, max(sub)), partition_size=512)
         full = ak.paged_decode(q, kc, vc, tables, lens, max(ctx), partition_size=512)
         lines.append(f"decode {(out.float() - full.float()).abs().max().item()}")
@@ -75,6 +75,11 @@ def _worker(rank, world, port, result_path):
         out_b = cp(q2, kc, vc, bt_local, lens_local, max(1, max(sub)), partition_size=512)
         full_b = ak.paged_decode(q2, kc, vc, tables, lens, max(ctx), partition_size=512)
         lines.append(f"second {(out_b.float() - full_b.float()).abs().max().item()}")
+        # The exchange over peer memory fused with the merge (two calls: both areas).
+        cpp = ContextParallelDecode(exchange="peer")
+        for tag, qq, ref in (("peer", q, full), ("peer2", q2, full_b)):
+            got = cpp(qq, kc, vc, bt_local, lens_local, max(1, max(sub)), partition_size=512)
+            lines.append(f"{tag} {(got.float() - ref.float()).abs().max().item()}")
         # The batch in chunks, exchange of one chunk overlapping the next one's decode.
         out2 = ContextParallelDecode(chunks=3)(q, kc, vc, bt_local, lens_local, max(1, max(sub)),
                                                partition_size=512)
@@ -114,5 +119,7 @@ def test_context_parallel_decode_two_gpus(tmp_path):
         vals = dict(line.split() for line in text.splitlines())
         assert float(vals["decode"]) < MAX_ABS, (r, text)
         assert float(vals["second"]) < MAX_ABS, (r, text)
+        assert float(vals["peer"]) < MAX_ABS, (r, text)
+        assert float(vals["peer2"]) < MAX_ABS, (r, text)
         assert float(vals["chunked"]) < MAX_ABS, (r, text)
         assert float(vals["prefill"]) == 0.0, (r, text)
