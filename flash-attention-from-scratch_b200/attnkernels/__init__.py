@@ -56,8 +56,9 @@ _MAX_SPLITS = 32
 
 def _decode_warps_per_sm(group):
     """Warps per CTA (one CTA per SM) of the decode kernel for G query heads per kv
-    head: 12 for G = 2 and 4, else 8 (DecCfg in csrc/decode.cu)."""
-    return 12 if group in (2, 4) else 8
+    head: 8 for every G (DecCfg in csrc/decode.cu)."""
+    del group
+    return _DECODE_WARPS_PER_SM
 
 
 @functools.lru_cache(maxsize=None)

@@ -22,12 +22,17 @@
 //     bs = 16, D = 128), so every copy is a long contiguous DRAM burst and
 //     128 KB of K and V per SM is in flight at D = 128. The producer runs
 //     `STAGES` stages ahead of the consumer, across unit boundaries.
-//   * No tensor cores (one query row per head): scores with 8 lanes per token
-//     and 16-byte shared-memory loads, an online softmax per 16-token stage,
-//     and P V with each lane owning D / 32 output columns. Grouped-query heads
-//     (G = H / H_kv) share every K/V byte; with G > 1 the partial dots are
-//     reduce-scattered so each lane runs the softmax of one head, and the
-//     probabilities reach P V through a small shared-memory buffer.
+//   * G = 1 (one query row per kv head) needs no tensor cores: scores with 8
+//     lanes per token and 16-byte shared-memory loads, an online softmax per
+//     16-token stage, and P V with each lane owning D / 32 output columns.
+//   * G > 1 (G = H / H_kv query heads share every K/V byte) does G times the
+//     arithmetic per byte, which the CUDA cores cannot hide under the stream:
+//     the G heads become the rows of a 16-row mma.sync tile (m16n8k16, rows
+//     past G zero), K and V fragments come from shared memory by ldmatrix
+//     (transposed for V), and each lane runs the softmax of its head's row on
+//     the accumulator fragment it holds. K and V arrive one token row per
+//     bulk copy, each row 16 bytes past a multiple of 128, so the 8 rows an
+//     ldmatrix reads hit 8 different bank groups.
 #include <algorithm>
 #include <mutex>
 
@@ -38,40 +43,51 @@ namespace fab {
 namespace {
 
 constexpr int kTok = 16;           // tokens per pipeline stage
-constexpr int kMinLaunchBatch = 512;  // fewest sequences any configuration takes per launch
+constexpr int kMinLaunchBatch = 2048;  // sequences any configuration takes per launch
 
 enum : unsigned int { kSiteDecodeWait = 201, kSiteDecodeDrain = 202, kSiteBadBlock = 203 };
 
-// Warps per CTA: 12 for G = 2 and 4, where the consumer's arithmetic per byte
-// makes it latency-bound at two warps per scheduler and its registers still
-// allow three; else 8 (G = 1 streams at the HBM roofline with 8; G = 8 needs
-// 255 registers). With 12 the ring holds two stages per warp and a launch takes
-// up to 512 sequences (their prefix sums live in shared memory).
+// Token rows per bulk copy in the G > 1 ring. Measured on B200 at 64 sequences
+// x 8192 tokens, 32 query over 8 kv heads, d 128 (us per launch): 1 row 467,
+// 2 rows 375, 4 rows 352, 8 rows 422, 16 rows 700. Fewer, larger copies issue
+// faster; more rows per group put more of an ldmatrix's 8 rows in one bank group.
+#ifndef FAB_DEC_CP
+#define FAB_DEC_CP 4
+#endif
+
+// Eight warps per CTA. G = 1 streams K and V at the HBM roofline with CUDA-core
+// arithmetic. G > 1 (query heads sharing a kv head) puts the scores and P V on
+// the tensor cores (mma.sync m16n8k16, fp16 in, fp32 accumulate, one 16-row
+// tile with the G heads as rows). Its ring stores a stage's 16 token rows in
+// groups of CP consecutive rows (one bulk copy each), the groups GS = CP ROW + 16
+// bytes apart: token t sits at (t / CP) GS + (t % CP) ROW, so rows of tokens in
+// different groups start in different 16-byte bank groups.
 template <int D, int G>
 struct DecCfg {
-  static constexpr int W = (G == 2 || G == 4) ? 12 : 8;
+  static constexpr bool MMA = G > 1;
+  static constexpr int W = 8;
   static constexpr int THREADS = W * 32;
-  static constexpr int MAXB = W == 12 ? kMinLaunchBatch : 2048;  // sequences per launch
+  static constexpr int MAXB = 2048;                        // sequences per launch
   static constexpr int ROW = D * 2;                        // bytes of one token of one head
-  static constexpr int KV = kTok * ROW;                    // K (or V) bytes of one stage
+  static constexpr int CP = MMA ? FAB_DEC_CP : kTok;       // token rows per copy group
+  static constexpr int NGRP = kTok / CP;                   // copy groups per stage and tensor
+  static constexpr int GS = CP * ROW + (MMA ? 16 : 0);     // ring bytes per copy group
+  static constexpr int KV = NGRP * GS;                     // K (or V) bytes of one stage
   static constexpr int QB = (G * D * 2 + 15) / 16 * 16;    // q bytes of one unit
   static constexpr int STAGE = 2 * KV + QB;
-  static constexpr int BUDGET = (W == 12 ? 210 : 196) * 1024 / W;  // ring bytes per warp
+  static constexpr int BUDGET = 196 * 1024 / W;            // ring bytes per warp
   static constexpr int STAGES = std::max(2, std::min(6, BUDGET / STAGE));
   static constexpr int RING = STAGES * STAGE;
   static constexpr int BAR_OFF = W * RING;
   static constexpr int META_OFF = BAR_OFF + W * STAGES * 8;
   static constexpr int PREFIX_OFF = META_OFF + W * STAGES * 16;
   static constexpr int CTX_OFF = PREFIX_OFF + (MAXB + 1) * 4;
-  // G > 1: per warp a buffer of the stage's probabilities P [kTok][G] and
-  // rescale factors alpha [G] (fp32), read back as broadcasts by every lane.
-  static constexpr int PBUF = ((kTok + 1) * G * 4 + 15) / 16 * 16;
-  static constexpr int P_OFF = (CTX_OFF + MAXB * 4 + 15) / 16 * 16;
-  static constexpr int SMEM = P_OFF + (G > 1 ? W * PBUF : 0) + 16;
-  static constexpr int E = D / 8;    // K elements per lane in the score phase
-  static constexpr int DV = D / 32;  // output columns per lane
+  static constexpr int SMEM = (CTX_OFF + MAXB * 4 + 15) / 16 * 16 + 16;  // + the abort flag
+  static constexpr int E = D / 8;    // K elements per lane in the score phase (G = 1)
+  static constexpr int DV = D / 32;  // output columns per lane (G = 1)
   static_assert(STAGES >= 2, "ring needs two stages");
   static_assert(SMEM <= 227 * 1024, "shared memory per CTA");
+  static_assert(!MMA || G <= 8, "one 16-row MMA tile holds the heads");
 };
 
 struct DecParams {
@@ -95,34 +111,33 @@ struct DecParams {
 };
 
 
-// Sums N partial values over the 8 lanes of a token group (lane bits 4, 2, 1 of
-// l8) and scatters them, in N - 1 shuffles instead of 3 N for N separate
-// butterflies. The lane's values come permuted: v[i] is value i ^ own, own =
-// l8 >> (3 - log2 N), so at every level a lane keeps the first half and sends the
-// second, which its partner (own differing in that level's bit) holds as its own
-// first half. Returns the full sum of value `own`.
-template <int N>
-__device__ __forceinline__ float scatter_sum8(const float (&v)[N]) {
-  static_assert(N == 2 || N == 4 || N == 8, "two to eight values");
-  constexpr int H1 = N / 2;
-  float w[H1];
-#pragma unroll
-  for (int i = 0; i < H1; ++i) w[i] = v[i] + __shfl_xor_sync(0xffffffffu, v[H1 + i], 4);
-  if constexpr (N == 2) {
-    float x = w[0];
-    x += __shfl_xor_sync(0xffffffffu, x, 2);
-    return x + __shfl_xor_sync(0xffffffffu, x, 1);
-  } else {
-    constexpr int H2 = N / 4;
-    float u[H2];
-#pragma unroll
-    for (int i = 0; i < H2; ++i) u[i] = w[i] + __shfl_xor_sync(0xffffffffu, w[H2 + i], 2);
-    if constexpr (N == 4) {
-      return u[0] + __shfl_xor_sync(0xffffffffu, u[0], 1);
-    } else {
-      return u[0] + __shfl_xor_sync(0xffffffffu, u[1], 1);
-    }
-  }
+// ldmatrix of four 8x8 fp16 matrices; lanes 8 i .. 8 i + 7 give the row
+// addresses of matrix i (16 bytes each, 16-byte aligned).
+__device__ __forceinline__ void ldmatrix_x4(uint32_t (&r)[4], uint32_t addr) {
+  asm volatile("ldmatrix.sync.aligned.m8n8.x4.shared.b16 {%0, %1, %2, %3}, [%4];"
+               : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3])
+               : "r"(addr));
+}
+
+__device__ __forceinline__ void ldmatrix_x4_trans(uint32_t (&r)[4], uint32_t addr) {
+  asm volatile("ldmatrix.sync.aligned.m8n8.x4.trans.shared.b16 {%0, %1, %2, %3}, [%4];"
+               : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3])
+               : "r"(addr));
+}
+
+// D[0:8, 0:8] += A[0:8, 0:16] B[0:16, 0:8] with mma.sync m16n8k16 (fp16 in,
+// fp32 accumulate) whose rows 8..15 are zero: the lane passes its row-g
+// fragments a0 (columns 2 t + {0, 1}) and a2 (columns 8 + 2 t + {0, 1}) and its
+// row-g accumulators d0, d1; the instruction's rows 8..15 get zeros in and are
+// dropped.
+__device__ __forceinline__ void mma_16816_rows8(float& d0, float& d1, uint32_t a0, uint32_t a2,
+                                                uint32_t b0, uint32_t b1) {
+  asm volatile(
+      "{\n\t.reg .f32 u0, u1;\n\t"
+      "mma.sync.aligned.m16n8k16.row.col.f32.f16.f16.f32 {%0, %1, u0, u1}, "
+      "{%2, %3, %4, %3}, {%5, %6}, {%0, %1, %7, %7};\n\t}"
+      : "+f"(d0), "+f"(d1)
+      : "r"(a0), "r"(0u), "r"(a2), "r"(b0), "r"(b1), "f"(0.f));
 }
 
 template <int D, int G>
@@ -223,9 +238,53 @@ __global__ void __launch_bounds__(DecCfg<D, G>::THREADS, 1) paged_decode_kernel(
     uint64_t* bar = full + slot;
     const int t0 = pstart + pst * kTok;
     const int nt = min(kTok, pend - t0);
+    const int rows_copied = C::MMA ? kTok : nt;
     if (lane == 0)
-      mbar_arrive_expect_tx(bar, 2 * nt * C::ROW + (pst == 0 ? G * D * 2 : 0));
+      mbar_arrive_expect_tx(bar, 2 * rows_copied * C::ROW + (pst == 0 ? G * D * 2 : 0));
     const int* btrow = p.bt + static_cast<size_t>(pb) * p.max_blocks;
+    if constexpr (C::MMA) {
+      // Lane r (and r + 16) looks up token row r of the stage (rows past a
+      // partial stage's last token repeat it: the tensor-core P V reads all 16
+      // rows, with P = 0 there, so a stage never holds another unit's data).
+      // Lanes [0, NGRP) then copy the K groups, lanes [16, 16 + NGRP) the V
+      // groups: one bulk copy when the group's rows are consecutive in one page,
+      // else one per row. The stage spans at most 16 pages, inside one 32-entry
+      // window of the block table.
+      const int pg_first = t0 / p.bs, pg_last = (t0 + nt - 1) / p.bs;
+      if (pg_last - bt_base >= 32 || pg_first < bt_base) {
+        bt_base = pg_first;
+        bt_reg = (pg_first + lane < p.max_blocks) ? btrow[pg_first + lane] : 0;
+      }
+      const int r = lane & 15;
+      const int t = t0 + min(r, nt - 1);
+      const int pg = t / p.bs;
+      int page = __shfl_sync(0xffffffffu, bt_reg, pg - bt_base);
+      if (page < 0 || page >= p.num_blocks) {  // never read outside the cache
+        if (r < nt) report_status(p.status, 2u /* ATTN_DEVICE_BAD_BLOCK */, kSiteBadBlock);
+        page = 0;
+      }
+      const long long eoff = static_cast<long long>(page) * p.block_stride +
+                             (static_cast<long long>(pkvh) * p.bs + (t - pg * p.bs)) * D;
+      const int gi = r < C::NGRP ? r : 0;
+      long long eo[C::CP];
+      bool whole = true;
+#pragma unroll
+      for (int i = 0; i < C::CP; ++i) {
+        eo[i] = __shfl_sync(0xffffffffu, eoff, gi * C::CP + i);
+        whole = whole && eo[i] == eo[0] + i * D;
+      }
+      __syncwarp();  // the expected bytes are set before any copy completes
+      if (r < C::NGRP) {
+        const __half* base = lane < 16 ? p.kc : p.vc;
+        uint8_t* dst = st + (lane < 16 ? 0 : C::KV) + r * C::GS;
+        if (whole) {
+          bulk_g2s(dst, base + eo[0], C::CP * C::ROW, bar);
+        } else {
+#pragma unroll
+          for (int i = 0; i < C::CP; ++i) bulk_g2s(dst + i * C::ROW, base + eo[i], C::ROW, bar);
+        }
+      }
+    } else {
     for (int t = t0; t < t0 + nt;) {
       const int pg = t / p.bs;
       const int off = t - pg * p.bs;
@@ -248,6 +307,7 @@ __global__ void __launch_bounds__(DecCfg<D, G>::THREADS, 1) paged_decode_kernel(
       }
       t += rows;
     }
+    }
     if (lane == 0) {
       if (pst == 0)
         bulk_g2s(st + 2 * C::KV, p.q + (static_cast<size_t>(pb) * p.hq + pkvh * G) * D,
@@ -260,183 +320,123 @@ __global__ void __launch_bounds__(DecCfg<D, G>::THREADS, 1) paged_decode_kernel(
   };
 
   // ---------------------------------------------------------- consumer state
-  // q * scale * log2(e) as packed fp32 pairs: the 16 (or 8) elements this lane
-  // multiplies in the score phase; slot g holds head g ^ hown (the order
-  // scatter_sum8 takes; hown = 0 for G = 1).
-  uint64_t qf[G][C::E / 2];
-  float m[G], l[G];  // G = 1 only (G > 1 keeps m_own, l_own below)
-  // Output columns [lane * DV, lane * DV + DV) as DV / 2 packed pairs. With
-  // G <= 2 two accumulator sets (even / odd tokens) halve the FMA chains.
-  constexpr int NACC = G <= 2 ? 2 : 1;
-  uint64_t acc[NACC][G][C::DV / 2];
-  // G > 1: after the reduce-scatter each lane holds the scores of one head
-  // (hown) and that head's running max and sum; the accumulators pair two heads
-  // per column, (head 2i, head 2i + 1) for column lane * DV + j, so the packed
-  // FMA takes the two heads' probabilities straight from shared memory.
-  constexpr int LG = G == 1 ? 0 : (G == 2 ? 1 : (G == 4 ? 2 : 3));
-  constexpr int HP = G > 1 ? G / 2 : 1;
-  const int hown = l8 >> (3 - LG);
-  const bool p_writer = (l8 & ((8 >> LG) - 1)) == 0;
-  float* pbuf = reinterpret_cast<float*>(smem + C::P_OFF) + warp * (C::PBUF / 4);
-  float m_own = -INFINITY, l_own = 0.f;
-  uint64_t acc2[NACC][HP][C::DV];
+  // G = 1: q * scale * log2(e) as packed fp32 pairs, the 16 (or 8) elements this
+  // lane multiplies in the score phase; running max and sum; output columns
+  // [lane * DV, lane * DV + DV) as DV / 2 packed pairs, in two accumulator sets
+  // (even / odd tokens) to halve the FMA chains.
+  uint64_t qf[C::MMA ? 1 : G][C::E / 2];
+  float m[G], l[G];
+  constexpr int NACC = 2;
+  uint64_t acc[C::MMA ? 1 : NACC][G][C::DV / 2];
 
   auto half2_pair = [](uint32_t h2) {
     const float2 f = __half22float2(*reinterpret_cast<const __half2*>(&h2));
     return f2_pack(f.x, f.y);
   };
 
+  // G > 1: mma.sync m16n8k16 with the G query heads as the rows of one 16-row
+  // tile (rows G..15 zero). Lane = (group g = lane / 4, t4 = lane % 4) holds, in
+  // the fragment layouts of that instruction, row g: q as A fragments (a0, a2
+  // per 16-element k-step; a1 = a3 = 0), the scores of tokens 2 t4, 2 t4 + 1
+  // (+ 8) and the output columns 8 n + 2 t4, 8 n + 2 t4 + 1 of every 8-column
+  // n-tile. Rows g >= G compute zeros and are not written.
+  constexpr int KS = D / 16, NT = D / 8;
+  const int g4 = lane >> 2, t4 = lane & 3;
+  uint32_t qa[C::MMA ? KS : 1][2];
+  float oc[C::MMA ? NT : 1][2];
+  float m_r = -INFINITY, l_r = 0.f;  // row g's running max (log2 units) and sum
+
   // One stage of a unit with G > 1 query heads per kv head (st: the stage's
   // ring slot, nt: its tokens, md: its unit and flags).
-  auto consume_grouped = [&](const uint8_t* st, int nt, const int4 md) {
-   if constexpr (G > 1) {
-    // Scores: token 4 * step + grp, 8 lanes per token; the G partial dots of a
-    // lane are summed over its token's 8 lanes and scattered, one head per lane.
-    float s1[kTok / 4];
-    const __half* kst = reinterpret_cast<const __half*>(st);
+  auto consume_mma = [&](const uint8_t* st, int nt, const int4 md) {
+   if constexpr (C::MMA) {
+    // Token columns: n-tile 0 holds the stage's even tokens, n-tile 1 the odd
+    // ones (column j of tile n is token 2 j + n), so the 8 rows of every
+    // ldmatrix spread over all 16 / CP copy groups (with CP = 4: two rows in
+    // each, a 2-way bank conflict).
+    // Scores S [heads x 16 tokens]: B = K rows read by ldmatrix, two k-steps per
+    // x4 load.
+    const uint32_t kst = smem_u32(st), vst = smem_u32(st + C::KV);
+    auto row_off = [](int tok) { return (tok / C::CP) * C::GS + (tok % C::CP) * C::ROW; };
+    float s[2][2] = {{0.f, 0.f}, {0.f, 0.f}};
 #pragma unroll
-    for (int step = 0; step < kTok / 4; ++step) {
-      const int t = step * 4 + grp;
-      uint64_t kf[C::E / 2];
+    for (int ks = 0; ks < KS; ks += 2) {
 #pragma unroll
-      for (int e8 = 0; e8 < C::E / 8; ++e8) {
-        const uint4 raw = *reinterpret_cast<const uint4*>(kst + t * D + e8 * 64 + l8 * 8);
-        kf[e8 * 4 + 0] = half2_pair(raw.x);
-        kf[e8 * 4 + 1] = half2_pair(raw.y);
-        kf[e8 * 4 + 2] = half2_pair(raw.z);
-        kf[e8 * 4 + 3] = half2_pair(raw.w);
+      for (int n = 0; n < 2; ++n) {
+        uint32_t b[4];
+        ldmatrix_x4(b, kst + row_off(2 * (lane & 7) + n) + (16 * ks + 8 * (lane >> 3)) * 2);
+        mma_16816_rows8(s[n][0], s[n][1], qa[ks][0], qa[ks][1], b[0], b[1]);
+        mma_16816_rows8(s[n][0], s[n][1], qa[ks + 1][0], qa[ks + 1][1], b[2], b[3]);
       }
-      float dot[G];
-#pragma unroll
-      for (int g = 0; g < G; ++g) {
-        uint64_t d0 = f2_mul(qf[g][0], kf[0]);
-        uint64_t d1 = f2_mul(qf[g][1], kf[1]);
-#pragma unroll
-        for (int e = 2; e < C::E / 2; e += 2) {
-          d0 = f2_fma(qf[g][e], kf[e], d0);
-          d1 = f2_fma(qf[g][e + 1], kf[e + 1], d1);
-        }
-        float a, b;
-        f2_unpack(f2_add(d0, d1), a, b);
-        dot[g] = a + b;
-      }
-      const float v = scatter_sum8<G>(dot);
-      s1[step] = (t < nt) ? v : -INFINITY;
     }
-    // Online softmax of this lane's head over the stage's 16 tokens (4 token groups).
-    float mx = fmaxf(fmaxf(s1[0], s1[1]), fmaxf(s1[2], s1[3]));
-    mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, 8));
-    mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, 16));
-    const float mn = fmaxf(m_own, mx);
-    const float alpha = fast_exp2(m_own - mn);
+    // Online softmax of row g over the stage's tokens (the 4 lanes of a group
+    // hold its 16 scores), in log2 units.
+    float mx = -INFINITY;
+#pragma unroll
+    for (int n = 0; n < 2; ++n)
+#pragma unroll
+      for (int c = 0; c < 2; ++c) {
+        const int tok = 2 * (2 * t4 + c) + n;
+        s[n][c] = tok < nt ? s[n][c] * p.scale_log2 : -INFINITY;
+        mx = fmaxf(mx, s[n][c]);
+      }
+    mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, 1));
+    mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, 2));
+    const float mn = fmaxf(m_r, mx);
+    const float alpha = fast_exp2(m_r - mn);
     float ps = 0.f;
 #pragma unroll
-    for (int step = 0; step < kTok / 4; ++step) {
-      s1[step] = fast_exp2(s1[step] - mn);
-      ps += s1[step];
-    }
-    ps += __shfl_xor_sync(0xffffffffu, ps, 8);
-    ps += __shfl_xor_sync(0xffffffffu, ps, 16);
-    l_own = l_own * alpha + ps;
-    m_own = mn;
-    // P [token][head] and alpha [head] to the warp's buffer. The __syncwarp after
-    // the last read of the previous stage keeps a lane that runs ahead from
-    // overwriting what another still reads.
-    float* pb = pbuf;
-    if (p_writer) {
+    for (int n = 0; n < 2; ++n)
 #pragma unroll
-      for (int step = 0; step < kTok / 4; ++step) pb[(step * 4 + grp) * G + hown] = s1[step];
-      if (grp == 0) pb[kTok * G + hown] = alpha;
-    }
-    __syncwarp();
-    const uint64_t* al = reinterpret_cast<const uint64_t*>(pb + kTok * G);
-#pragma unroll
-    for (int i = 0; i < HP; ++i) {
-      const uint64_t a2 = al[i];
-#pragma unroll
-      for (int a = 0; a < NACC; ++a)
-#pragma unroll
-        for (int j = 0; j < C::DV; ++j) acc2[a][i][j] = f2_mul(acc2[a][i][j], a2);
-    }
-    // P V: lane owns columns [lane * DV, lane * DV + DV) of every head. A partial
-    // stage skips the missing tokens, whose shared-memory rows hold stale data.
-    const __half* vst = reinterpret_cast<const __half*>(st + C::KV) + lane * C::DV;
-    auto pv = [&](int t) {
-      float vf[C::DV];
-      if constexpr (C::DV == 4) {
-        const uint2 raw = *reinterpret_cast<const uint2*>(vst + t * D);
-        const float2 x = __half22float2(*reinterpret_cast<const __half2*>(&raw.x));
-        const float2 y = __half22float2(*reinterpret_cast<const __half2*>(&raw.y));
-        vf[0] = x.x; vf[1] = x.y; vf[2] = y.x; vf[3] = y.y;
-      } else {
-        const uint32_t raw = *reinterpret_cast<const uint32_t*>(vst + t * D);
-        const float2 x = __half22float2(*reinterpret_cast<const __half2*>(&raw));
-        vf[0] = x.x; vf[1] = x.y;
+      for (int c = 0; c < 2; ++c) {
+        s[n][c] = fast_exp2(s[n][c] - mn);
+        ps += s[n][c];
       }
-      const uint64_t* pp = reinterpret_cast<const uint64_t*>(pb + t * G);
-      uint64_t pr[HP];
+    ps += __shfl_xor_sync(0xffffffffu, ps, 1);
+    ps += __shfl_xor_sync(0xffffffffu, ps, 2);
+    l_r = l_r * alpha + ps;
+    m_r = mn;
+    if (__any_sync(0xffffffffu, alpha != 1.f)) {
 #pragma unroll
-      for (int i = 0; i < HP; ++i) pr[i] = pp[i];
-#pragma unroll
-      for (int j = 0; j < C::DV; ++j) {
-        const uint64_t vv = f2_pack(vf[j], vf[j]);
-#pragma unroll
-        for (int i = 0; i < HP; ++i) acc2[t % NACC][i][j] = f2_fma(pr[i], vv, acc2[t % NACC][i][j]);
+      for (int n = 0; n < NT; ++n) {
+        oc[n][0] *= alpha;
+        oc[n][1] *= alpha;
       }
-    };
-    if (nt == kTok) {
-#pragma unroll
-      for (int t = 0; t < kTok; ++t) pv(t);
-    } else {
-#pragma unroll
-      for (int t = 0; t < kTok; ++t)
-        if (t < nt) pv(t);
     }
-    __syncwarp();
-    if (md.w & 64) {
+    // O += P V: A = P (fp16, from the score fragments: k slots 0-7 the even
+    // tokens, 8-15 the odd ones), B = V with the same k order, n = columns, read
+    // by transposing ldmatrix, two n-tiles per load.
+    const uint32_t pa0 = pack_half2(s[0][0], s[0][1]);
+    const uint32_t pa2 = pack_half2(s[1][0], s[1][1]);
+#pragma unroll
+    for (int n = 0; n < NT; n += 2) {
+      uint32_t b[4];
+      ldmatrix_x4_trans(b, vst + row_off(2 * (lane & 7) + ((lane >> 3) & 1)) +
+                               (8 * n + 8 * (lane >> 4)) * 2);
+      mma_16816_rows8(oc[n][0], oc[n][1], pa0, pa2, b[0], b[1]);
+      mma_16816_rows8(oc[n + 1][0], oc[n + 1][1], pa0, pa2, b[2], b[3]);
+    }
+    if ((md.w & 64) && g4 < G) {
       const int b = md.x, kvh = md.y, split = md.z;
       const int ns = min((ctx_s[b] + p.partition - 1) / p.partition, p.num_splits);
-      float o[G][C::DV];
+      const float inv = 1.f / l_r;
+      const size_t row = static_cast<size_t>(b) * p.hq + kvh * G + g4;
+      if (p.direct_out && ns == 1) {
+        uint32_t* dst = reinterpret_cast<uint32_t*>(p.out + row * D + 2 * t4);
 #pragma unroll
-      for (int i = 0; i < HP; ++i)
+        for (int n = 0; n < NT; ++n) dst[4 * n] = pack_half2(oc[n][0] * inv, oc[n][1] * inv);
+      } else {
+        const size_t pr = row * p.num_splits + split;
+        float2* dst = reinterpret_cast<float2*>(p.o_part + pr * D + 2 * t4);
 #pragma unroll
-        for (int j = 0; j < C::DV; ++j) {
-          uint64_t v = acc2[0][i][j];
-          if constexpr (NACC == 2) v = f2_add(v, acc2[1][i][j]);
-          f2_unpack(v, o[2 * i][j], o[2 * i + 1][j]);
-        }
-#pragma unroll
-      for (int g = 0; g < G; ++g) {
-        const int src = g << (3 - LG);  // a lane of token group 0 that holds head g
-        const float lg = __shfl_sync(0xffffffffu, l_own, src);
-        const float mg = __shfl_sync(0xffffffffu, m_own, src);
-        const float inv = 1.f / lg;
-#pragma unroll
-        for (int j = 0; j < C::DV; ++j) o[g][j] *= inv;
-        const size_t row = static_cast<size_t>(b) * p.hq + kvh * G + g;
-        if (p.direct_out && ns == 1) {
-          __half* dst = p.out + row * D + lane * C::DV;
-          if constexpr (C::DV == 4) {
-            *reinterpret_cast<uint2*>(dst) =
-                make_uint2(pack_half2(o[g][0], o[g][1]), pack_half2(o[g][2], o[g][3]));
-          } else {
-            *reinterpret_cast<uint32_t*>(dst) = pack_half2(o[g][0], o[g][1]);
-          }
-        } else {
-          const size_t pr = row * p.num_splits + split;
-          float* dst = p.o_part + pr * D + lane * C::DV;
-          if constexpr (C::DV == 4) {
-            *reinterpret_cast<float4*>(dst) = make_float4(o[g][0], o[g][1], o[g][2], o[g][3]);
-          } else {
-            *reinterpret_cast<float2*>(dst) = make_float2(o[g][0], o[g][1]);
-          }
-          if (lane == 0) {
-            p.m_part[pr] = mg;
-            p.l_part[pr] = lg;
-          }
+        for (int n = 0; n < NT; ++n) dst[4 * n] = make_float2(oc[n][0] * inv, oc[n][1] * inv);
+        if (t4 == 0) {
+          p.m_part[pr] = m_r;
+          p.l_part[pr] = l_r;
         }
       }
     }
+    __syncwarp();
    }
   };
 
@@ -449,6 +449,25 @@ __global__ void __launch_bounds__(DecCfg<D, G>::THREADS, 1) paged_decode_kernel(
     const int4 md = meta[slot];
     const uint8_t* st = ring + slot * C::STAGE;
     const int nt = md.w & 31;
+    if constexpr (C::MMA) {
+      if (md.w & 32) {
+        // q of the unit as A fragments (rows = heads; rows >= G zero), fp16 as
+        // stored; the scale is applied to the fp32 scores.
+        const __half* qs = reinterpret_cast<const __half*>(st + 2 * C::KV);
+#pragma unroll
+        for (int ks = 0; ks < KS; ++ks) {
+          const bool real = g4 < G;
+          qa[ks][0] = real ? *reinterpret_cast<const uint32_t*>(qs + g4 * D + 16 * ks + 2 * t4) : 0u;
+          qa[ks][1] =
+              real ? *reinterpret_cast<const uint32_t*>(qs + g4 * D + 16 * ks + 8 + 2 * t4) : 0u;
+        }
+        m_r = -INFINITY;
+        l_r = 0.f;
+#pragma unroll
+        for (int n = 0; n < NT; ++n) oc[n][0] = oc[n][1] = 0.f;
+      }
+      consume_mma(st, nt, md);
+    } else {
     if (md.w & 32) {
       const __half* qs = reinterpret_cast<const __half*>(st + 2 * C::KV);
       const uint64_t sc = f2_pack(p.scale_log2, p.scale_log2);
@@ -456,35 +475,20 @@ __global__ void __launch_bounds__(DecCfg<D, G>::THREADS, 1) paged_decode_kernel(
       for (int g = 0; g < G; ++g) {
 #pragma unroll
         for (int e8 = 0; e8 < C::E / 8; ++e8) {
-          const uint4 raw = *reinterpret_cast<const uint4*>(qs + (g ^ hown) * D + e8 * 64 + l8 * 8);
+          const uint4 raw = *reinterpret_cast<const uint4*>(qs + g * D + e8 * 64 + l8 * 8);
           qf[g][e8 * 4 + 0] = f2_mul(half2_pair(raw.x), sc);
           qf[g][e8 * 4 + 1] = f2_mul(half2_pair(raw.y), sc);
           qf[g][e8 * 4 + 2] = f2_mul(half2_pair(raw.z), sc);
           qf[g][e8 * 4 + 3] = f2_mul(half2_pair(raw.w), sc);
         }
-        if constexpr (G == 1) {
-          m[g] = -INFINITY;
-          l[g] = 0.f;
-#pragma unroll
-          for (int a = 0; a < NACC; ++a)
-#pragma unroll
-            for (int j = 0; j < C::DV / 2; ++j) acc[a][g][j] = f2_pack(0.f, 0.f);
-        }
-      }
-      if constexpr (G > 1) {
-        m_own = -INFINITY;
-        l_own = 0.f;
+        m[g] = -INFINITY;
+        l[g] = 0.f;
 #pragma unroll
         for (int a = 0; a < NACC; ++a)
 #pragma unroll
-          for (int i = 0; i < HP; ++i)
-#pragma unroll
-            for (int j = 0; j < C::DV; ++j) acc2[a][i][j] = f2_pack(0.f, 0.f);
+          for (int j = 0; j < C::DV / 2; ++j) acc[a][g][j] = f2_pack(0.f, 0.f);
       }
     }
-    if constexpr (G > 1) {
-      consume_grouped(st, nt, md);
-    } else {
     // Scores: token 4 * step + grp, 8 lanes per token, two FMA chains per head.
     float s[kTok / 4][G];
     const __half* kst = reinterpret_cast<const __half*>(st);
