@@ -662,7 +662,8 @@ def bench_long_context(args, d: Dist, peaks, peak_src, traffic):
     torch.cuda.empty_cache()
 
     # Config 5: each sequence's context split into block-aligned ranges, one per
-    # rank; partials merged across ranks (one NCCL all-gather per step).
+    # rank; partials merged across ranks (by default one kernel that pushes them to
+    # every peer over NVLink and merges; --cp-exchange nccl: an NCCL all-gather).
     c = CFG5
     t0, t1 = parallel.context_range(c["ctx"], c["block_size"], d.world, d.rank)
     local = [t1 - t0] * c["batch"]
@@ -688,7 +689,10 @@ def bench_long_context(args, d: Dist, peaks, peak_src, traffic):
     t5 = traffic.get("paged_decode_kernel_cfg5_per_token")
     out["config5_decode"] = {
         "workload": "paged decode B=8 H=32 d=128 ctx=131072, context ranges over ranks, "
-                    "NCCL all-gather + merge of the (o, m, l) partials",
+                    + ("(o, m, l) partials exchanged over NVLink peer memory and merged in one "
+                       "kernel" if args.cp_exchange == "peer" and d.world > 1 else
+                       "NCCL all-gather + merge of the (o, m, l) partials" if d.world > 1 else
+                       "one rank: split-K decode + merge"),
         "tokens_per_rank": t1 - t0, "partition": part, "scaling": "strong",
         "ms_per_step": round(ms / args.steps, 4),
         "value": round(total / (ms / args.steps * 1e-3) / 1e9, 1), "unit": "GB/s",

@@ -1,11 +1,13 @@
-"""Context-parallel paged decode across 2 GPUs over NCCL, with the CUDA kernels.
+"""Context-parallel paged decode across 2, 4 and 8 GPUs, with the CUDA kernels.
 
 Each rank holds the blocks of its block-aligned slice of every sequence's
 context, computes the (o, m, l) partials with attn_paged_decode_partials, the
-partials are all-gathered over NCCL and merged with attn_merge_partials. Every
-rank's result must match single-GPU paged_decode over the whole context. Also
+partials are exchanged (all-gathered over NCCL and merged with
+attn_merge_partials, or pushed over NVLink peer memory and merged in one kernel
+by attn_exchange_merge_partials) and every rank's result must match single-GPU
+paged_decode over the whole context. Also
 checks head-sharded prefill: each rank's heads equal the same heads computed on
-one GPU. Skipped on hosts with fewer than two GPUs.
+one GPU. Each world size is skipped on hosts with fewer GPUs.
 """
 import datetime
 import os
@@ -99,9 +101,10 @@ def _worker(rank, world, port, result_path):
     Path(f"{result_path}.{rank}").write_text("\n".join(lines))
 
 
-@pytest.mark.skipif(torch.cuda.device_count() < 2, reason="needs two GPUs")
-def test_context_parallel_decode_two_gpus(tmp_path):
-    world = 2
+@pytest.mark.parametrize("world", [2, 4, 8])
+def test_context_parallel_decode(tmp_path, world):
+    if torch.cuda.device_count() < world:
+        pytest.skip(f"needs {world} GPUs")
     port = _free_port()
     res = str(tmp_path / "res")
     ctx = mp.get_context("spawn")
