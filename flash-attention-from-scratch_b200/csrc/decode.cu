@@ -154,6 +154,9 @@ __global__ void __launch_bounds__(DecCfg<D, G>::THREADS, 1) paged_decode_kernel(
   int* prefix = reinterpret_cast<int*>(smem + C::PREFIX_OFF);
   int* ctx_s = reinterpret_cast<int*>(smem + C::CTX_OFF);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(smem + C::SMEM - 16);
+  // The merge launch that follows may be scheduled now; it waits for this
+  // launch's completion before it reads the partials.
+  asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
 
   // Context lengths and the prefix sums of the splits per sequence: active
   // (sequence, split) pairs are numbered densely, v in [0, prefix[batch]).
@@ -660,8 +663,18 @@ struct MergeParams {
 
 // WPR warps per row (1 or 8): a CTA of 8 warps merges 8 / WPR rows, and the
 // warps of one row take contiguous ranges of its parts. Lane owns D / 32
-// consecutive columns. With many parts per row (a long context cut into many
-// splits, few rows) eight warps keep eight times as many part rows in flight.
+// consecutive columns. A warp walks its parts in chunks of 8, loading the
+// chunk's m, l and o rows at once and folding them into a running
+// (max, sum, numerator) like the online softmax, so the loads of a warp's parts
+// are one round trip per chunk; the warps of a row then combine their states in
+// shared memory, each rescaled to the row's max. With many parts per row (a long
+// context cut into many splits, few rows) eight warps keep eight times as many
+// part rows in flight.
+//
+// The kernel is launched as a programmatic dependent of the decode launch before
+// it: it may start while that launch runs and waits (griddepcontrol.wait) for
+// its completion before reading the partials. context_lens, an input of the
+// decode launch, is read before the wait.
 template <int D, int WPR>
 __global__ void __launch_bounds__(256) merge_partials_kernel(const MergeParams p) {
   constexpr int DV = D / 32;
@@ -677,78 +690,98 @@ __global__ void __launch_bounds__(256) merge_partials_kernel(const MergeParams p
     ns = min((c + p.partition - 1) / p.partition, p.num_parts);
   }
   if (live && p.skip_single && ns == 1) live = false;
+  asm volatile("griddepcontrol.wait;" ::: "memory");
   if constexpr (WPR == 1) {
     if (!live) return;
   }
-  float mx = -INFINITY;
-  float num[DV];
+  float mw = -INFINITY;  // running max of this warp's parts
+  float den = 0.f;       // sum of l_s 2^(m_s - mw)
+  float num[DV];         // sum of l_s 2^(m_s - mw) o_s, this lane's columns
 #pragma unroll
   for (int j = 0; j < DV; ++j) num[j] = 0.f;
-  float den = 0.f;
   if (live) {
     const float* mrow = p.m + row * p.ml_row_stride;
     const float* lrow = p.l + row * p.ml_row_stride;
-    for (int s = lane; s < ns; s += 32) mx = fmaxf(mx, mrow[s * p.ml_part_stride]);
-    mx = warp_max(mx);
+    const float* orow = p.o + row * p.o_row_stride + lane * DV;
     const int per = (ns + WPR - 1) / WPR;
     const int s_begin = min(ns, sub * per);
     const int s_end = min(ns, s_begin + per);
-    if (mx != -INFINITY) {
-      // Parts in groups of 32: lane s holds the weight of part s0 + s; the
-      // weights are broadcast by shuffles while eight part rows are loaded at
-      // once, so the loads of a row's parts overlap instead of forming a chain.
-      const float* orow = p.o + row * p.o_row_stride + lane * DV;
-      for (int s0 = s_begin; s0 < s_end; s0 += 32) {
-        const int cnt = min(32, s_end - s0);
-        float wl = 0.f;
-        if (lane < cnt)
-          wl = lrow[(s0 + lane) * p.ml_part_stride] *
-               fast_exp2(mrow[(s0 + lane) * p.ml_part_stride] - mx);
-        den += wl;
-        for (int t0 = 0; t0 < cnt; t0 += 8) {
-          float v[8][DV];
-          float w[8];
+    for (int s0 = s_begin; s0 < s_end; s0 += 8) {
+      const int cnt = min(8, s_end - s0);
+      // Lane u holds m and l of part s0 + u % 8 (the four octets alike).
+      const bool have = (lane & 7) < cnt;
+      const long long su = static_cast<long long>(s0 + (lane & 7)) * p.ml_part_stride;
+      const float mu = have ? mrow[su] : -INFINITY;
+      const float lu = have ? lrow[su] : 0.f;
+      float v[8][DV];
 #pragma unroll
-          for (int u = 0; u < 8; ++u) {
-            const int t = t0 + u;
-            w[u] = __shfl_sync(0xffffffffu, wl, t & 31);
-            const float* src = orow + static_cast<long long>(s0 + t) * p.o_part_stride;
-            if (t < cnt) {
-              if constexpr (DV == 4) {
-                const float4 x = *reinterpret_cast<const float4*>(src);
-                v[u][0] = x.x; v[u][1] = x.y; v[u][2] = x.z; v[u][3] = x.w;
-              } else {
-                const float2 x = *reinterpret_cast<const float2*>(src);
-                v[u][0] = x.x; v[u][1] = x.y;
-              }
-            } else {
-#pragma unroll
-              for (int j = 0; j < DV; ++j) v[u][j] = 0.f;
-              w[u] = 0.f;
-            }
+      for (int u = 0; u < 8; ++u) {
+        const float* src = orow + static_cast<long long>(s0 + u) * p.o_part_stride;
+        if (u < cnt) {
+          if constexpr (DV == 4) {
+            const float4 x = *reinterpret_cast<const float4*>(src);
+            v[u][0] = x.x; v[u][1] = x.y; v[u][2] = x.z; v[u][3] = x.w;
+          } else {
+            const float2 x = *reinterpret_cast<const float2*>(src);
+            v[u][0] = x.x; v[u][1] = x.y;
           }
+        } else {
 #pragma unroll
-          for (int u = 0; u < 8; ++u)
-#pragma unroll
-            for (int j = 0; j < DV; ++j) num[j] = fmaf(w[u], v[u][j], num[j]);
+          for (int j = 0; j < DV; ++j) v[u][j] = 0.f;
         }
       }
-      den = warp_sum(den);
+      float cm = mu;
+      cm = fmaxf(cm, __shfl_xor_sync(0xffffffffu, cm, 1));
+      cm = fmaxf(cm, __shfl_xor_sync(0xffffffffu, cm, 2));
+      cm = fmaxf(cm, __shfl_xor_sync(0xffffffffu, cm, 4));
+      const float mn = fmaxf(mw, cm);
+      if (mn == -INFINITY) continue;  // no context in these parts, nor before
+      const float alpha = fast_exp2(mw - mn);
+      const float wu = lu * fast_exp2(mu - mn);
+      float ws = wu;
+      ws += __shfl_xor_sync(0xffffffffu, ws, 1);
+      ws += __shfl_xor_sync(0xffffffffu, ws, 2);
+      ws += __shfl_xor_sync(0xffffffffu, ws, 4);
+      den = den * alpha + ws;
+#pragma unroll
+      for (int j = 0; j < DV; ++j) num[j] *= alpha;
+#pragma unroll
+      for (int u = 0; u < 8; ++u) {
+        const float w = __shfl_sync(0xffffffffu, wu, u);
+#pragma unroll
+        for (int j = 0; j < DV; ++j) num[j] = fmaf(w, v[u][j], num[j]);
+      }
+      mw = mn;
     }
   }
   if constexpr (WPR > 1) {
-    // The row's warps add their sums in shared memory; the first one writes.
-    __shared__ float red[8][D + 1];
+    // The row's warps combine their states in shared memory; the first one writes.
+    __shared__ float red[8][D + 2];
 #pragma unroll
     for (int j = 0; j < DV; ++j) red[warp][lane * DV + j] = num[j];
-    if (lane == 0) red[warp][D] = den;
+    if (lane == 0) {
+      red[warp][D] = den;
+      red[warp][D + 1] = mw;
+    }
     __syncthreads();
     if (!live || sub != 0) return;
-    for (int w = 1; w < WPR; ++w) {
+    float mrow_max = mw;
+    for (int w = 1; w < WPR; ++w) mrow_max = fmaxf(mrow_max, red[warp + w][D + 1]);
+    if (mrow_max == -INFINITY) {
+      den = 0.f;
+    } else {
+      const float a0 = fast_exp2(mw - mrow_max);
+      den *= a0;
 #pragma unroll
-      for (int j = 0; j < DV; ++j) num[j] += red[warp + w][lane * DV + j];
-      den += red[warp + w][D];
+      for (int j = 0; j < DV; ++j) num[j] *= a0;
+      for (int w = 1; w < WPR; ++w) {
+        const float a = fast_exp2(red[warp + w][D + 1] - mrow_max);
+        den = fmaf(a, red[warp + w][D], den);
+#pragma unroll
+        for (int j = 0; j < DV; ++j) num[j] = fmaf(a, red[warp + w][lane * DV + j], num[j]);
+      }
     }
+    mw = mrow_max;
   }
   const float inv = den > 0.f ? 1.f / den : 0.f;
   if (p.out16 != nullptr) {
@@ -764,7 +797,7 @@ __global__ void __launch_bounds__(256) merge_partials_kernel(const MergeParams p
 #pragma unroll
     for (int j = 0; j < DV; ++j) dst[j] = num[j] * inv;
     if (lane == 0) {
-      p.out_m[row] = mx;
+      p.out_m[row] = mw;
       p.out_l[row] = den;
     }
   }
@@ -861,23 +894,34 @@ cudaError_t dispatch_group(int g, const DecParams& prm, int64_t upper, const Lau
   }
 }
 
+// Launched as a programmatic dependent of the stream's previous kernel (the
+// kernel waits for it before reading any partial).
+template <int D, int WPR>
+cudaError_t launch_merge_kernel(const MergeParams& mp, unsigned grid, cudaStream_t stream) {
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3(grid);
+  cfg.blockDim = dim3(256);
+  cfg.dynamicSmemBytes = 0;
+  cfg.stream = stream;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  return cudaLaunchKernelEx(&cfg, merge_partials_kernel<D, WPR>, mp);
+}
+
 cudaError_t launch_merge_impl(const MergeParams& mp, int d, cudaStream_t stream) {
   if (mp.rows == 0) return cudaSuccess;
   // Eight warps per row from 32 parts up (at least four parts per warp).
   if (mp.num_parts >= 32) {
     const unsigned grid = static_cast<unsigned>(mp.rows);
-    if (d == 64)
-      merge_partials_kernel<64, 8><<<grid, 256, 0, stream>>>(mp);
-    else
-      merge_partials_kernel<128, 8><<<grid, 256, 0, stream>>>(mp);
-  } else {
-    const unsigned grid = static_cast<unsigned>((mp.rows + 7) / 8);
-    if (d == 64)
-      merge_partials_kernel<64, 1><<<grid, 256, 0, stream>>>(mp);
-    else
-      merge_partials_kernel<128, 1><<<grid, 256, 0, stream>>>(mp);
+    return d == 64 ? launch_merge_kernel<64, 8>(mp, grid, stream)
+                   : launch_merge_kernel<128, 8>(mp, grid, stream);
   }
-  return cudaGetLastError();
+  const unsigned grid = static_cast<unsigned>((mp.rows + 7) / 8);
+  return d == 64 ? launch_merge_kernel<64, 1>(mp, grid, stream)
+                 : launch_merge_kernel<128, 1>(mp, grid, stream);
 }
 
 }  // namespace
