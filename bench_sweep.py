@@ -226,18 +226,19 @@ def run_prefill(h, rows, quick, backends):
 # ------------------------------------------------------------------- decode
 
 
-def decode_rows(h, section, ctx_lens, impls_wanted, partition=None, seed=0, **extra):
-    """Rows of one decode case (all requested implementations on the same cache)."""
+def decode_rows(h, section, seq_lens, impls_wanted, partition=None, seed=0, **extra):
+    """Rows of one decode case (all requested implementations on the same cache); `extra`
+    adds fields to every row (the ragged section records its `ctx_lens`)."""
     import attnkernels as ak
 
-    b = len(ctx_lens)
-    kc, vc, tables, lens = bench.synthetic_paged_cache(ctx_lens, DEC_HKV, DEC_D, DEC_BS, seed,
+    b = len(seq_lens)
+    kc, vc, tables, lens = bench.synthetic_paged_cache(seq_lens, DEC_HKV, DEC_D, DEC_BS, seed,
                                                        h.device)
     q = bench.randn_half((b, DEC_HQ, DEC_D),
                          torch.Generator(device=h.device).manual_seed(seed + 1), h.device)
-    top = max(ctx_lens)
+    top = max(seq_lens)
     n_blocks = -(-top // DEC_BS)
-    ragged = len(set(ctx_lens)) > 1
+    ragged = len(set(seq_lens)) > 1
     part = partition or ak.decode_partition(b, DEC_HKV, top, num_heads=DEC_HQ)
     impls = {
         "paged_split": lambda: ak.paged_decode(q, kc, vc, tables, lens, top,
@@ -253,8 +254,8 @@ def decode_rows(h, section, ctx_lens, impls_wanted, partition=None, seed=0, **ex
         q_rows = q.view(b, DEC_HKV, DEC_HQ // DEC_HKV, DEC_D)
         impls["torch_sdpa_contiguous"] = lambda: F.scaled_dot_product_attention(q_rows, k_flat,
                                                                                 v_flat)
-    want = decode_fp32_first(q, kc, vc, tables, ctx_lens[0])
-    nbytes = decode_kv_bytes(ctx_lens)
+    want = decode_fp32_first(q, kc, vc, tables, seq_lens[0])
+    nbytes = decode_kv_bytes(seq_lens)
     out = []
     for impl in impls_wanted:
         fn = impls.get(impl)
@@ -268,7 +269,7 @@ def decode_rows(h, section, ctx_lens, impls_wanted, partition=None, seed=0, **ex
             torch.cuda.empty_cache()
             continue
         gbps, frac = h.rate("hbm", nbytes, ms)
-        row = dict(section=section, impl=impl, batch=b, ctx=top, ctx_mean=sum(ctx_lens) / b,
+        row = dict(section=section, impl=impl, batch=b, ctx=top, ctx_mean=sum(seq_lens) / b,
                    heads=DEC_HQ, kv_heads=DEC_HKV, head_dim=DEC_D, block_size=DEC_BS,
                    ms=round(ms, 4), gbps=round(gbps, 1), frac=frac, n_gpus=1, sm_mhz=mhz,
                    max_abs_err=float(f"{err:.3g}"), **extra)

@@ -35,6 +35,25 @@ def test_decode_checks_match_oracle():
                        ref.gather_kv(kc, tables, nblk))
 
 
+def test_section_drivers_call_decode_rows_with_its_signature(monkeypatch):
+    """Every decode section's call binds to decode_rows' parameters (the ragged
+    section adds its ctx_lens field to the rows)."""
+    import inspect
+
+    sig = inspect.signature(bench_sweep.decode_rows)
+    calls = []
+
+    def fake(*args, **kwargs):
+        calls.append(sig.bind(*args, **kwargs))
+        return []
+
+    monkeypatch.setattr(bench_sweep, "decode_rows", fake)
+    rows = []
+    for run in (bench_sweep.run_decode, bench_sweep.run_split_ablation, bench_sweep.run_ragged):
+        run(None, rows, True)
+    assert calls and calls[-1].arguments["extra"]["ctx_lens"] == calls[-1].arguments["seq_lens"]
+
+
 def test_kv_bytes_convention():
     # K and V, fp16, 8 kv heads of 128: the reference's bench/bench.py:199-200.
     assert bench_sweep.decode_kv_bytes([1024, 2048]) == 3072 * 8 * 128 * 4
