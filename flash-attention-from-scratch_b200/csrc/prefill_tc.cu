@@ -130,6 +130,15 @@ struct TcCfg {
   static_assert(NQ == 2, "the register split assumes two softmax warpgroups");
   static_assert(128 * CONTROL_REGS + 256 * SOFTMAX_REGS <= THREADS * LAUNCH_REGS, "register split");
   static constexpr int O_COL = NQ * kBN;  // first O column; S_i at i * kBN
+  // At D = 64 the next S_i is computed in two N = 64 halves and P_i (packed
+  // fp16, 64 columns) is written over the second half of S_i, so the first
+  // half of the next S_i (keys 0-63) runs while P_i V still reads P_i.
+  // Measured on B200: config 2 at d 64 +2.5 %; at D = 128 the N = 64 S MMAs
+  // are shared-memory bound (an SS 128x64x16 MMA reads 6 KB) and the split
+  // costs 12 %, so there the whole S_i follows P_i V and P_i sits in the first
+  // half.
+  static constexpr bool SPLIT_S = D == 64;
+  static constexpr int P_COL = SPLIT_S ? kBN / 2 : 0;
   static constexpr int TMEM_COLS = pow2_ceil(NQ * (kBN + D));
   static_assert(TMEM_COLS <= 512, "tensor memory holds 512 columns");
   static_assert(SMEM_ALLOC <= 227 * 1024, "shared memory per CTA");
@@ -358,6 +367,7 @@ __global__ void __launch_bounds__(TcCfg<D, NQ>::THREADS, 1)
     // group of MMAs and commits is then issued by one elected lane.
     {
       constexpr uint32_t kIdescS = idesc_f16_f32(kBM, kBN, false, false);
+      constexpr uint32_t kIdescS64 = idesc_f16_f32(kBM, kBN / 2, false, false);
       constexpr uint32_t kIdescO = idesc_f16_f32(kBM, D, false, true);
       // Descriptors are built once; a K step or a stage moves the start
       // address field (address / 16, bits 0-13), which never carries out
@@ -383,6 +393,19 @@ __global__ void __launch_bounds__(TcCfg<D, NQ>::THREADS, 1)
           mma_f16_ss(tmem + i * kBN, a0 + off, b0 + off, kIdescS, kk > 0 ? 1u : 0u);
         }
       };
+      // Keys [64 h, 64 h + 64) of S_i into TMEM columns [64 h, 64 h + 64) of S_i
+      // (N = 64; the K rows start 64 rows = 8 KB into each 64-column block).
+      auto issue_s_half = [&](int i, int st, int h) {
+        const uint64_t a0 = q_desc + i * kTileStep;
+        const uint64_t b0 = k_desc0 + static_cast<uint32_t>(st) * kStageStep + h * (8192 >> 4);
+#pragma unroll
+        for (int kk = 0; kk < D / 16; ++kk) {
+          constexpr uint32_t kBlk = C::BLK_BYTES >> 4;
+          const uint32_t off = (kk >> 2) * kBlk + (kk & 3) * 2;
+          mma_f16_ss(tmem + i * kBN + h * (kBN / 2), a0 + off, b0 + off, kIdescS64,
+                     kk > 0 ? 1u : 0u);
+        }
+      };
       // O_i (+)= P_i V: K = 128 keys in steps of 16 rows (2 KB of V); V is
       // MN-major, the 64-column blocks 16 KB apart (LBO), 8-row groups 1 KB (SBO).
       // Half h covers keys [64 h, 64 h + 64): P columns [32 h, 32 h + 32).
@@ -390,7 +413,7 @@ __global__ void __launch_bounds__(TcCfg<D, NQ>::THREADS, 1)
         const uint64_t b0 = v_desc0 + static_cast<uint32_t>(st) * kStageStep;
 #pragma unroll
         for (int kk = 4 * h; kk < 4 * h + 4; ++kk) {
-          mma_f16_ts(tmem + C::O_COL + i * D, tmem + i * kBN + kk * 8, b0 + kk * (2048 >> 4),
+          mma_f16_ts(tmem + C::O_COL + i * D, tmem + i * kBN + C::P_COL + kk * 8, b0 + kk * (2048 >> 4),
                      kIdescO, (accumulate || kk > 0) ? 1u : 0u);
         }
       };
@@ -461,6 +484,8 @@ __global__ void __launch_bounds__(TcCfg<D, NQ>::THREADS, 1)
               if (elect_one()) {
                 issue_pv(i, st, 0, j > 0);
                 if (pending >= 0) tc_commit(stage_free + pending);
+                // Keys 0-63 of the next S go to columns P_i does not occupy.
+                if (C::SPLIT_S && next && j + 1 < nkv[i]) issue_s_half(i, st, 0);
               }
               __syncwarp();
               pending = -1;
@@ -470,15 +495,15 @@ __global__ void __launch_bounds__(TcCfg<D, NQ>::THREADS, 1)
               if (elect_one()) {
                 issue_pv(i, st, 1, true);
                 if (j + 1 == nkv[i]) tc_commit(o_full + i);  // O_i final
-              }
-              __syncwarp();
-              if (next && j + 1 < nkv[i]) {
-                if (elect_one()) {
-                  issue_s(i, st);  // K_{j+1}
+                if (next && j + 1 < nkv[i]) {
+                  if (C::SPLIT_S)
+                    issue_s_half(i, st, 1);  // keys 64-127 of S_i(j + 1), over P_i
+                  else
+                    issue_s(i, st);  // K_{j+1}
                   tc_commit(s_full + i);
                 }
-                __syncwarp();
               }
+              __syncwarp();
               par ^= 1u << i;
             }
           }
@@ -635,14 +660,14 @@ __global__ void __launch_bounds__(TcCfg<D, NQ>::THREADS, 1)
 #pragma unroll
               for (int c = 0; c < kBN / 4; ++c) exp_pair(c);
             }
-            tmem_st32<0>(t_s, sr);
+            tmem_st32<0>(t_s + C::P_COL, sr);
             tmem_st_wait();
             tc_fence_before();
             __syncwarp();
             if (lane == 0) mbar_arrive(p_full + 2 * wg);
 #pragma unroll
             for (int c = kBN / 4; c < kBN / 2; ++c) exp_pair(c);
-            tmem_st32<32>(t_s + 32, sr);
+            tmem_st32<32>(t_s + C::P_COL + 32, sr);
             tmem_st_wait();
             tc_fence_before();
             __syncwarp();
