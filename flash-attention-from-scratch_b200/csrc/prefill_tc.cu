@@ -22,8 +22,8 @@
 //     stages at D = 128), so the MMA warp waits once and commits once per step.
 //   * S_i = Q_i K^T is a tcgen05.mma with both operands in shared memory and the
 //     fp32 result in tensor memory (TMEM). The softmax thread of row r reads row
-//     r of S_i from TMEM lane r, writes P as packed fp16 back over the first 64
-//     columns of S_i, and O_i += P_i V is a tcgen05.mma with A = P read from
+//     r of S_i from TMEM lane r, writes P as packed fp16 back over 64 of the
+//     128 columns of S_i, and O_i += P_i V is a tcgen05.mma with A = P read from
 //     TMEM and B = V from shared memory (MN-major), accumulating in TMEM.
 //   * The two query tiles ping-pong: while one warpgroup does its softmax the
 //     tensor core runs the other tile's products.
