@@ -80,6 +80,35 @@ def test_odd_block_sizes(bs):
     assert mx < MAX_ABS and mean < MEAN_ABS
 
 
+@pytest.mark.parametrize("d", [64, 128])
+@pytest.mark.parametrize("heads", [(8, 4), (16, 2)])
+@pytest.mark.parametrize("bs", [1, 3, 4, 24, 64])
+def test_grouped_odd_block_sizes(d, heads, bs):
+    """G = 2 and 8 (the tensor-core consumer) with pages that split 4-token copy groups
+    and 16-token stages, and partial last stages (17, 50, 300 tokens)."""
+    mx, mean = run([300, 50, 17, 1], heads[0], heads[1], d, bs=bs)
+    assert mx < MAX_ABS and mean < MEAN_ABS
+
+
+@pytest.mark.parametrize("heads", [(8, 2), (8, 8)])
+def test_partial_stages_never_read_other_units(heads):
+    """Thousands of short units per launch, so every warp's ring is reused across
+    units: sequences whose V holds +inf (their own outputs are not finite) next to
+    sequences whose last stage is partial. The rows of a partial stage past its last
+    token must not hold another unit's V, or P = 0 times inf would turn into NaN."""
+    n = 2000
+    ctx = [48 if b % 2 == 0 else 21 for b in range(n)]
+    k_cache, v_cache, tables, lens = cache(ctx, heads[1], 64, seed=11)
+    for b in range(0, n, 2):
+        v_cache[tables[b, 0], :, 5, :] = float("inf")
+    q = torch.randn(n, heads[0], 64, device="cuda").half()
+    out = ak.paged_decode(q, k_cache, v_cache, tables, lens, 48)
+    clean = torch.arange(1, n, 2, device="cuda")
+    assert torch.isfinite(out[clean]).all()
+    ref = oracle(q[clean], k_cache, v_cache, tables[clean], lens[clean])
+    assert max_err(out[clean], ref) < MAX_ABS and mean_err(out[clean], ref) < MEAN_ABS
+
+
 def test_long_context_split():
     mx, mean = run([32768], 32, 8, 128)
     assert mx < ATOL
