@@ -691,6 +691,10 @@ __global__ void __launch_bounds__(256) merge_partials_kernel(const MergeParams p
   }
   if (live && p.skip_single && ns == 1) live = false;
   asm volatile("griddepcontrol.wait;" ::: "memory");
+  // A programmatic dependent launched after this kernel (the exchange of
+  // context-parallel decode) may be scheduled now; it waits for this kernel's
+  // completion before it reads the merged partials.
+  asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
   if constexpr (WPR == 1) {
     if (!live) return;
   }

@@ -64,6 +64,9 @@ __global__ void __launch_bounds__(256) exchange_merge_kernel(const XParams p) {
   const int warp = threadIdx.x >> 5;
   const int lane = threadIdx.x & 31;
   __shared__ int failed;
+  // Launched as a programmatic dependent of the kernel that writes this rank's
+  // partials: nothing is read or written before that kernel has completed.
+  asm volatile("griddepcontrol.wait;" ::: "memory");
   const long long o_floats = static_cast<long long>(p.rows) * D;
   const float* mine = p.slots[p.rank] + p.rank * p.slot_stride;  // own slot in own area
   for (int blk = blockIdx.x; blk < p.num_blocks; blk += gridDim.x) {
@@ -170,11 +173,18 @@ cudaError_t launch_exchange_merge(float* const* slots, unsigned int* const* flag
   p.num_blocks = static_cast<int>((rows + 7) / 8);
   p.epoch = epoch;
   const int grid = std::max(1, std::min(p.num_blocks, ctx.sm_count));
-  if (d == 64)
-    exchange_merge_kernel<64><<<grid, 256, 0, ctx.stream>>>(p);
-  else
-    exchange_merge_kernel<128><<<grid, 256, 0, ctx.stream>>>(p);
-  return cudaGetLastError();
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3(grid);
+  cfg.blockDim = dim3(256);
+  cfg.dynamicSmemBytes = 0;
+  cfg.stream = ctx.stream;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  return d == 64 ? cudaLaunchKernelEx(&cfg, exchange_merge_kernel<64>, p)
+                 : cudaLaunchKernelEx(&cfg, exchange_merge_kernel<128>, p);
 }
 
 }  // namespace fab
