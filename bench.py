@@ -700,12 +700,18 @@ def bench_long_context(args, d: Dist, peaks, peak_src, traffic):
     if d.world > 1:
         # The same step without the exchange: this rank's partials alone (decode kernel +
         # local split-K merge), to name what the exchange and the merge across ranks add.
+        # Three interleaved rounds of both, medians: one pair of runs is within the
+        # run-to-run noise of the difference.
         partials = lambda: ak.paged_decode_partials(q, kc, vc, tables, lens, t1 - t0,  # noqa: E731
                                                     partition_size=part)
-        ms_local = timed(partials, args.steps, args.warmup, d)
-        out["config5_decode"]["local_partials_ms_per_step"] = round(ms_local / args.steps, 4)
-        out["config5_decode"]["exchange_and_merge_ms_per_step"] = round(
-            (ms - ms_local) / args.steps, 4)
+        full_r, local_r = [], []
+        for _ in range(3):
+            full_r.append(timed(fn, args.steps, args.warmup, d) / args.steps)
+            local_r.append(timed(partials, args.steps, args.warmup, d) / args.steps)
+        ms_full, ms_local = statistics.median(full_r), statistics.median(local_r)
+        out["config5_decode"]["local_partials_ms_per_step"] = round(ms_local, 4)
+        out["config5_decode"]["full_step_ms_median_of_3"] = round(ms_full, 4)
+        out["config5_decode"]["exchange_and_merge_ms_per_step"] = round(ms_full - ms_local, 4)
         nbytes = c["batch"] * c["heads"] * (c["head_dim"] + 2) * 4
         out["config5_decode"]["exchange"] = (
             f"peer memory: each rank stores its {nbytes} bytes of partials into every peer over "
