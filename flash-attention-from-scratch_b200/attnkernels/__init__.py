@@ -54,11 +54,12 @@ _DECODE_WARPS_PER_SM = 8
 _MAX_SPLITS = 32
 
 
-def _decode_warps_per_sm(group):
+def _decode_warps_per_sm(group, head_dim=128):
     """Warps per CTA (one CTA per SM) of the decode kernel for G query heads per kv
-    head: 8 for every G (DecCfg in csrc/decode.cu)."""
+    head: 16 at head_dim 64, whose 2 KB stages make each warp latency-bound, 8 at
+    128, for every G (DecCfg in csrc/decode.cu)."""
     del group
-    return _DECODE_WARPS_PER_SM
+    return 2 * _DECODE_WARPS_PER_SM if head_dim == 64 else _DECODE_WARPS_PER_SM
 
 
 @functools.lru_cache(maxsize=None)
@@ -109,34 +110,34 @@ def _sm_count(device_index):
 
 
 def decode_partition(batch, num_kv_heads, max_context_len, device=None, sm_count=None,
-                     num_heads=None):
+                     num_heads=None, head_dim=128):
     """Tokens per split for paged_decode.
 
     Same contract as attnkernels/__init__.py:93-101 (a multiple of CHUNK, at
     least one chunk per split, more splits when batch * kv heads is small), with
     the B200 target: about _UNITS_PER_WARP (sequence, kv head, split) units per
-    resident decode warp (8 per SM), so the persistent kernel balances ragged
-    batches, and at most _MAX_SPLITS * G splits per sequence, G = num_heads /
-    num_kv_heads (1 when num_heads is not given), which bounds the merge.
-    `sm_count` overrides the device query.
+    resident decode warp (8 per SM, 16 at head_dim 64), so the persistent kernel
+    balances ragged batches, and at most _MAX_SPLITS * G splits per sequence, G =
+    num_heads / num_kv_heads (1 when num_heads is not given), which bounds the
+    merge. `sm_count` overrides the device query.
     """
     if sm_count is None:
         dev = torch.cuda.current_device() if device is None else device
         sm_count = _sm_count(dev)
     group = max(1, num_heads // num_kv_heads) if num_heads else 1
     return _partition(int(batch), int(num_kv_heads), int(max_context_len), int(sm_count),
-                      group)
+                      group, int(head_dim))
 
 
 @functools.lru_cache(maxsize=4096)
-def _partition(batch, num_kv_heads, max_context_len, sm_count, group):
+def _partition(batch, num_kv_heads, max_context_len, sm_count, group, head_dim=128):
     seqs = max(1, batch * num_kv_heads)
     want = -(-_UNITS_PER_WARP * _DECODE_WARPS_PER_SM * sm_count // seqs)
     max_chunks = max(1, -(-max_context_len // CHUNK))
     cap = _MAX_SPLITS * group
     splits = max(1, min(want, max_chunks, cap))
     part = -(-max_chunks // splits) * CHUNK
-    warps = _decode_warps_per_sm(group) * sm_count
+    warps = _decode_warps_per_sm(group, head_dim) * sm_count
     if seqs * -(-max_context_len // part) >= 4 * warps:
         return part
     # Few units for the resident warps: the launch takes about (rounds of units per
@@ -179,7 +180,8 @@ def _decode_args(q, k_cache, v_cache, block_tables, context_lens, max_context_le
     scale = 1.0 / math.sqrt(q.shape[-1]) if scale is None else scale
     if partition_size is None:
         partition_size = decode_partition(q3.shape[0], k_cache.shape[1], max_context_len,
-                                          q.device.index, num_heads=q3.shape[1])
+                                          q.device.index, num_heads=q3.shape[1],
+                                          head_dim=q3.shape[2])
     partition_size = -(-int(partition_size) // CHUNK) * CHUNK
     return (q3.contiguous(), k_cache.contiguous(), v_cache.contiguous(),
             block_tables.to(device=q.device, dtype=torch.int32).contiguous(),

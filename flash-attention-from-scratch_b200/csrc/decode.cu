@@ -11,7 +11,8 @@
 //     M = max_s m_s,  w_s = l_s 2^(m_s - M),  O = sum_s w_s o_s / sum_s w_s.
 //
 // The B200 design is different from the reference's one-CTA-per-split grid:
-//   * A persistent grid of one CTA per SM, 8 warps per CTA. Each warp is an
+//   * A persistent grid of one CTA per SM, 8 warps per CTA (16 at head_dim
+//     64). Each warp is an
 //     independent pipeline that owns whole work units (sequence, kv head,
 //     split) and fetches the next unit from an atomic counter, so no CTA-wide
 //     barrier is ever taken inside the main loop and the short final splits of
@@ -51,12 +52,19 @@ enum : unsigned int { kSiteDecodeWait = 201, kSiteDecodeDrain = 202, kSiteBadBlo
 // x 8192 tokens, 32 query over 8 kv heads, d 128 (us per launch): 1 row 467,
 // 2 rows 375, 4 rows 352, 8 rows 422, 16 rows 700. Fewer, larger copies issue
 // faster; more rows per group put more of an ldmatrix's 8 rows in one bank group.
+// Warps per CTA at head_dim 64. A 16-token stage there is 4 KB of K and V, and a
+// warp's stage is latency-bound (about 0.2 instructions per cycle per warp), so
+// twice the warps of head_dim 128 keep HBM busy: 64 sequences x 8192 tokens, 8
+// kv heads, B200, 8 -> 16 warps: G = 1 276 -> 202 us, G = 4 297 -> 213 us.
+#ifndef FAB_DEC_W64
+#define FAB_DEC_W64 16
+#endif
 #ifndef FAB_DEC_CP
 #define FAB_DEC_CP 4
 #endif
 
-// Eight warps per CTA. G = 1 streams K and V at the HBM roofline with CUDA-core
-// arithmetic. G > 1 (query heads sharing a kv head) puts the scores and P V on
+// Eight warps per CTA at head_dim 128, 16 at 64. G = 1 streams K and V with
+// CUDA-core arithmetic. G > 1 (query heads sharing a kv head) puts the scores and P V on
 // the tensor cores (mma.sync m16n8k16, fp16 in, fp32 accumulate, one 16-row
 // tile with the G heads as rows). Its ring stores a stage's 16 token rows in
 // groups of CP consecutive rows (one bulk copy each), the groups GS = CP ROW + 16
@@ -65,7 +73,7 @@ enum : unsigned int { kSiteDecodeWait = 201, kSiteDecodeDrain = 202, kSiteBadBlo
 template <int D, int G>
 struct DecCfg {
   static constexpr bool MMA = G > 1;
-  static constexpr int W = 8;
+  static constexpr int W = D == 64 ? FAB_DEC_W64 : 8;
   static constexpr int THREADS = W * 32;
   static constexpr int MAXB = 2048;                        // sequences per launch
   static constexpr int ROW = D * 2;                        // bytes of one token of one head
