@@ -835,6 +835,14 @@ def profile_case(kind, d: Dist):
         part = ak.decode_partition(1, c["kv_heads"], c["ctx"])
         fn = lambda: ak.paged_decode(q, kc, vc, tables, lens, c["ctx"],  # noqa: E731
                                      partition_size=part)
+    elif kind == "decode_d64":
+        # head_dim 64 at the decode_gqa shape, one query head per kv head (8 and 8):
+        # 1.07 GB of K/V, partition 512.
+        ctx = [8192] * 64
+        kc, vc, tables, lens = synthetic_paged_cache(ctx, 8, 64, 16, 4200, d.device)
+        q = randn_half((64, 8, 64), torch.Generator(device=d.device).manual_seed(2), d.device)
+        fn = lambda: ak.paged_decode(q, kc, vc, tables, lens, 8192,  # noqa: E731
+                                     partition_size=512)
     elif kind == "decode_gqa":
         # The reference's results-table decode layer (32 query over 8 kv heads, d 128,
         # block 16) at 64 sequences of 8192 tokens: 2.1 GB of K/V, partition 512.
@@ -921,7 +929,7 @@ def main():
     ap.add_argument("--ablation", action="store_true",
                     help="print the decode split-size ablation (one JSON list) and exit")
     ap.add_argument("--profile", choices=["prefill", "prefill_d64", "prefill_n4095",
-                                          "prefill_long", "decode", "decode_gqa",
+                                          "prefill_long", "decode", "decode_gqa", "decode_d64",
                                           "decode_long"],
                     help="run one small case of a kernel (3 + 2 launches) for ncu, no timing")
     args = ap.parse_args()
