@@ -60,6 +60,12 @@ def test_decode_partition_contract():
     assert ak.decode_partition(64, 32, 8192, sm_count=148) == 512
     # One rank's share of config 5 at 8 GPUs (8 x 32 heads, 16384 tokens): 512.
     assert ak.decode_partition(8, 32, 16384, sm_count=148) == 512
+    # head_dim 64 runs twice the warps per SM: a contract-valid partition either way,
+    # and for these shapes no fewer splits than at head_dim 128.
+    for batch, hkv, ctx in [(1, 8, 32768), (16, 8, 4096), (64, 8, 8192)]:
+        p64 = ak.decode_partition(batch, hkv, ctx, sm_count=148, head_dim=64)
+        p128 = ak.decode_partition(batch, hkv, ctx, sm_count=148, head_dim=128)
+        assert p64 % ak.CHUNK == 0 and p64 <= p128
 
 
 def test_shard_range_partitions():
