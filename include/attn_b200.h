@@ -159,6 +159,10 @@ int attn_paged_decode_partials(const void* q, const void* k_cache, const void* v
  * m_parts/l_parts[p * ml_part_stride + r]. Rows whose parts all have l = 0
  * get zeros. The same merge as the reference's paged_reduce_kernel
  * (attnkernels/csrc/paged_decode.cu:196-216), applied across GPUs.
+ * The kernel is launched as a programmatic dependent of the previous kernel on
+ * `stream`: it may start while that kernel runs, and reads no partial before it
+ * has completed (the same holds for the merge inside attn_paged_decode and for
+ * attn_exchange_merge_partials).
  */
 int attn_merge_partials(const float* o_parts, const float* m_parts, const float* l_parts,
                         int64_t num_parts, int64_t rows, int64_t head_dim, int64_t o_part_stride,
