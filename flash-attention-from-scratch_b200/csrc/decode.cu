@@ -87,13 +87,17 @@ struct DecCfg {
   static constexpr int STAGES = std::max(2, std::min(6, BUDGET / STAGE));
   static constexpr int RING = STAGES * STAGE;
   static constexpr int BAR_OFF = W * RING;
-  static constexpr int META_OFF = BAR_OFF + W * STAGES * 8;
+  // The int4 stage descriptors need 16-byte alignment (an odd W * STAGES would
+  // leave the barriers' end 8 bytes past it).
+  static constexpr int META_OFF = (BAR_OFF + W * STAGES * 8 + 15) / 16 * 16;
   static constexpr int PREFIX_OFF = META_OFF + W * STAGES * 16;
   static constexpr int CTX_OFF = PREFIX_OFF + (MAXB + 1) * 4;
   static constexpr int SMEM = (CTX_OFF + MAXB * 4 + 15) / 16 * 16 + 16;  // + the abort flag
   static constexpr int E = D / 8;    // K elements per lane in the score phase (G = 1)
   static constexpr int DV = D / 32;  // output columns per lane (G = 1)
   static_assert(STAGES >= 2, "ring needs two stages");
+  static_assert(STAGE % 16 == 0 && BAR_OFF % 16 == 0 && META_OFF % 16 == 0,
+                "bulk copy, ldmatrix and int4 alignment of the shared-memory layout");
   static_assert(SMEM <= 227 * 1024, "shared memory per CTA");
   static_assert(!MMA || G <= 8, "one 16-row MMA tile holds the heads");
 };
